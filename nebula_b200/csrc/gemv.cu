@@ -1,0 +1,137 @@
+// Dense projections and element-wise operators of the qwen/gpu.h ABI:
+// qg_matmul, qg_gather, qg_dequant, qg_unary, qg_binary, qg_shared_add.
+//
+// qg_matmul keeps the reference's 32-lane accumulation order (one warp per
+// weight row, lane j owns columns j mod 32, then the 16/8/4/2/1 tree), so its
+// output is bitwise equal to qc_matmul (qwen/cpu.c:119-148). The router GEMV
+// that feeds top-10 selection relies on this for bit-exact expert ids.
+#include "quant.cuh"
+
+using namespace nb;
+
+namespace {
+constexpr int kRowsPerCta = 4;  // one warp per row
+constexpr int kTokTile = 16;    // token vectors per pass, kept in registers
+
+template <int T>
+__global__ void __launch_bounds__(kRowsPerCta * 32) matmul_kernel(float *out, const unsigned char *w, int type,
+                                                                  int rows, int cols, const float *x, int nt,
+                                                                  size_t stride) {
+    const int row = blockIdx.x * kRowsPerCta + (threadIdx.x >> 5);
+    const int first = blockIdx.y * kTokTile;
+    if (row >= rows) return;
+    const int n = min(kTokTile, nt - first);
+    const float *xs[kTokTile];
+#pragma unroll
+    for (int t = 0; t < kTokTile; t++) xs[t] = x + (size_t)(first + min(t, n - 1)) * cols;
+    float acc[kTokTile];
+#pragma unroll
+    for (int t = 0; t < kTokTile; t++) acc[t] = 0.0f;
+    const unsigned char *r = w + (size_t)row * stride;
+    if (T >= 0)
+        lane_dot<T, kTokTile>(r, cols, xs, n, acc);
+    else
+        lane_dot_generic<kTokTile>(r, type, cols, xs, n, acc);
+#pragma unroll
+    for (int t = 0; t < kTokTile; t++) {
+        if (t < n) {
+            float s = lane_tree(acc[t]);
+            if ((threadIdx.x & 31) == 0) out[(size_t)(first + t) * rows + row] = s;
+        }
+    }
+}
+
+__global__ void gather_kernel(float *out, const unsigned char *w, int type, int n, size_t stride, int row) {
+    int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) out[i] = decode_at(w + (size_t)row * stride, type, i);
+}
+
+__global__ void dequant_kernel(float *o, const unsigned char *w, int type, int rows, int cols, size_t stride) {
+    size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < (size_t)rows * cols) o[i] = decode_at(w + (i / cols) * stride, type, (int)(i % cols));
+}
+
+__global__ void unary_kernel(float *o, const float *x, int n, int op, float s) {
+    int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) {
+        float a = x[i] * s;
+        o[i] = op == 0 ? a * sigmoidf_ref(a) : op == 1 ? sigmoidf_ref(a) : a;
+    }
+}
+
+__global__ void binary_kernel(float *o, const float *a, const float *b, int n, int op) {
+    int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) o[i] = op == 0 ? a[i] + b[i] : a[i] * b[i];
+}
+
+__global__ void shared_add_kernel(float *o, const float *x, const float *g, int nt, int width) {
+    int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < nt * width) o[i] = __fmaf_rn(x[i], sigmoidf_ref(g[i / width]), o[i]);
+}
+
+bool valid_cols(int type, int cols) {
+    if (type == 12 || type == 13 || type == 14) return cols % 256 == 0;
+    if (type == 2 || type == 6 || type == 7 || type == 8 || type == 20) return cols % 32 == 0;
+    return true;
+}
+}  // namespace
+
+namespace nb {
+// Bit-exact GEMV launch shared with the MoE layer's router.
+int launch_matmul(float *o, const void *w, int type, int rows, int cols, const float *x, int nt, cudaStream_t st) {
+    size_t stride = row_bytes(type, cols);
+    if (!o || !w || !x || !stride || rows < 1 || cols < 1 || nt < 1 || nt > kMaxTokens || !valid_cols(type, cols))
+        return cudaErrorInvalidValue;
+    dim3 grid((rows + kRowsPerCta - 1) / kRowsPerCta, (nt + kTokTile - 1) / kTokTile);
+    const unsigned char *wb = static_cast<const unsigned char *>(w);
+    switch (type) {
+    case 0: matmul_kernel<0><<<grid, kRowsPerCta * 32, 0, st>>>(o, wb, type, rows, cols, x, nt, stride); break;
+    case 12: matmul_kernel<12><<<grid, kRowsPerCta * 32, 0, st>>>(o, wb, type, rows, cols, x, nt, stride); break;
+    case 20: matmul_kernel<20><<<grid, kRowsPerCta * 32, 0, st>>>(o, wb, type, rows, cols, x, nt, stride); break;
+    default: matmul_kernel<-1><<<grid, kRowsPerCta * 32, 0, st>>>(o, wb, type, rows, cols, x, nt, stride); break;
+    }
+    return cudaGetLastError();
+}
+}  // namespace nb
+
+extern "C" int qg_matmul(float *o, const void *w, int type, int rows, int cols, const float *x, int nt) {
+    return launch_matmul(o, w, type, rows, cols, x, nt, launch_stream);
+}
+
+extern "C" int qg_gather(float *o, const void *w, int type, int cols, int row) {
+    size_t stride = row_bytes(type, cols);
+    if (!o || !w || !stride || row < 0 || !valid_cols(type, cols)) return cudaErrorInvalidValue;
+    gather_kernel<<<(cols + 255) / 256, 256, 0, launch_stream>>>(o, static_cast<const unsigned char *>(w), type,
+                                                                  cols, stride, row);
+    return cudaGetLastError();
+}
+
+extern "C" int qg_dequant(float *o, const void *w, int type, int rows, int cols) {
+    size_t stride = row_bytes(type, cols);
+    if (!o || !w || !stride || rows < 1 || !valid_cols(type, cols)) return cudaErrorInvalidValue;
+    size_t n = (size_t)rows * cols;
+    dequant_kernel<<<(unsigned)((n + 255) / 256), 256, 0, launch_stream>>>(o, static_cast<const unsigned char *>(w),
+                                                                           type, rows, cols, stride);
+    return cudaGetLastError();
+}
+
+extern "C" int qg_unary(float *o, const float *x, int n, int op, float s) {
+    if (n < 0) return cudaErrorInvalidValue;
+    if (!n) return 0;
+    unary_kernel<<<(n + 255) / 256, 256, 0, launch_stream>>>(o, x, n, op, s);
+    return cudaGetLastError();
+}
+
+extern "C" int qg_binary(float *o, const float *a, const float *b, int n, int op) {
+    if (n < 0) return cudaErrorInvalidValue;
+    if (!n) return 0;
+    binary_kernel<<<(n + 255) / 256, 256, 0, launch_stream>>>(o, a, b, n, op);
+    return cudaGetLastError();
+}
+
+// Width 2560 is part of this entry point's contract (qwen/gpu.cu:552-553).
+extern "C" int qg_shared_add(float *o, const float *x, const float *g, int nt) {
+    if (nt < 1) return cudaErrorInvalidValue;
+    shared_add_kernel<<<(nt * 2560 + 255) / 256, 256, 0, launch_stream>>>(o, x, g, nt, 2560);
+    return cudaGetLastError();
+}

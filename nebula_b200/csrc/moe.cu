@@ -1,0 +1,904 @@
+// All-resident routed MoE for sm_100a: qg_moe_workspace_bytes, qg_moe_routed,
+// qg_moe_layer, qg_moe_status.
+//
+// One layer is a fixed sequence of kernels on the caller's stream, with no
+// host synchronisation (graph-capturable):
+//   plan     - one CTA validates the routes, counts tokens per expert and
+//              builds the expert-major pair list (ascending token order),
+//              replacing the host read of route ids (qwen/qwen.c:649-655) and
+//              the moe_map kernel (qwen/gpu.cu:489-505).
+//   gate_up  - grid (F/16 row tiles) x (used experts [+ shared]); each CTA
+//              stages 16 gate rows and 16 up rows of one expert in shared
+//              memory with TMA bulk copies and produces mid = SiLU(g)*u for
+//              every token routed to that expert (qwen/cpu.c:209-217).
+//   down     - grid (H/64 row tiles) x (used experts [+ shared]); weighted
+//              slot rows slots[t*10+k] = w[t][k] * (W_down mid)
+//              (qwen/cpu.c:219-225).
+//   combine  - out[t] = sum_{k=0..9} slots (rank order, from +0.0f), then the
+//              gated shared expert (qwen/cpu.c:227-231, qwen/gpu.cu:552).
+//
+// Dequant-dot formulation (both Q4_K and IQ4_NL): the scale of each 32-value
+// group is applied once per group instead of once per weight,
+//   sum_k w_k x_k = sum_g [ d*sc_g * sum_l q_l x_l  -  dmin*m_g * sum_l x_l ]
+// with the 4-bit codes q_l converted exactly. The per-group sums of x are
+// computed once per staged token. This is not the reference's summation
+// order, so routed outputs match qc_moe within the float tolerance rather
+// than bitwise; the router (ids) and qg_matmul stay bit-exact.
+#include <algorithm>
+#include <utility>
+#include <vector>
+#include "quant.cuh"
+
+using namespace nb;
+
+namespace nb {
+int launch_matmul(float *o, const void *w, int type, int rows, int cols, const float *x, int nt, cudaStream_t st);
+int launch_route(int *ids, float *weights, const float *logits, const float *bias, int nt, cudaStream_t st);
+}  // namespace nb
+
+namespace {
+
+// ---------------------------------------------------------------- profiling
+// Optional CUDA-event timing of each phase of the MoE layer (qg_moe_profile).
+// Only eager launches on the legacy stream are timed; graph captures are not.
+enum Phase { kRouter, kRoute, kPlan, kGateUp, kDown, kCombine, kPhases };
+struct Profiler {
+    bool on = false;
+    std::vector<cudaEvent_t> pool;
+    std::vector<std::pair<int, std::pair<cudaEvent_t, cudaEvent_t>>> spans;
+    size_t next = 0;
+    cudaEvent_t take() {
+        if (next == pool.size()) {
+            cudaEvent_t e = nullptr;
+            if (cudaEventCreate(&e) != cudaSuccess) return nullptr;
+            pool.push_back(e);
+        }
+        return pool[next++];
+    }
+};
+Profiler g_prof;
+
+struct Span {
+    int phase;
+    cudaEvent_t a = nullptr, b = nullptr;
+    cudaStream_t st;
+    Span(int p, cudaStream_t s) : phase(p), st(s) {
+        if (g_prof.on && st == 0 && (a = g_prof.take()) && (b = g_prof.take())) cudaEventRecord(a, st);
+    }
+    ~Span() {
+        if (a && b) {
+            cudaEventRecord(b, st);
+            g_prof.spans.push_back({phase, {a, b}});
+        }
+    }
+};
+
+constexpr int kThreads = 256;
+constexpr int kTP = 4;               // tokens per pass
+constexpr int kGateUpRows = 16;      // rows of gate (and of up) per CTA
+constexpr int kDownRows = 64;        // rows of down per CTA
+constexpr int kPlanChunk = 512;      // tokens per bitmap chunk in the plan kernel
+
+// ---------------------------------------------------------------- workspace
+struct Layout {
+    size_t hdr, counts, off, used, pairs, bad, logits, ids, wts, mid, slots, shared, total;
+};
+
+inline size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
+
+Layout layout(int T, int H, int F) {
+    Layout L{};
+    size_t p = 0;
+    auto take = [&](size_t bytes) {
+        size_t at = p;
+        p = align256(p + bytes);
+        return at;
+    };
+    L.hdr = take(64);
+    L.counts = take(sizeof(int) * kExperts);
+    L.off = take(sizeof(int) * (kExperts + 1));
+    L.used = take(sizeof(int) * kExperts);
+    L.pairs = take(sizeof(int) * (size_t)T * kTop);
+    L.bad = take(sizeof(int) * (size_t)T);
+    L.logits = take(sizeof(float) * (size_t)T * (kExperts + 1));
+    L.ids = take(sizeof(int) * (size_t)T * kTop);
+    L.wts = take(sizeof(float) * (size_t)T * kTop);
+    L.mid = take(sizeof(float) * ((size_t)T * kTop + T) * F);
+    L.slots = take(sizeof(float) * (size_t)T * kTop * H);
+    L.shared = take(sizeof(float) * (size_t)T * H);
+    L.total = p;
+    return L;
+}
+
+// Status words at the start of the workspace.
+struct Header {
+    int invalid_tokens;  // tokens given NaN output rows
+    int n_pairs;         // routed (token, expert) pairs computed
+    int n_used;          // distinct experts used
+    int error;           // bounded-wait timeouts or internal errors
+};
+
+struct Plan {
+    Header *hdr;
+    int *counts, *off, *used, *pairs, *bad;
+};
+
+Plan plan_ptrs(void *ws, const Layout &L) {
+    char *b = static_cast<char *>(ws);
+    return Plan{reinterpret_cast<Header *>(b + L.hdr), reinterpret_cast<int *>(b + L.counts),
+                reinterpret_cast<int *>(b + L.off),   reinterpret_cast<int *>(b + L.used),
+                reinterpret_cast<int *>(b + L.pairs), reinterpret_cast<int *>(b + L.bad)};
+}
+
+// ---------------------------------------------------------------- plan
+// Validation follows qc_moe (qwen/cpu.c:241-246): an omitted route is an id
+// in [-513,-2] with weight exactly 0; otherwise the id must be in [0,512),
+// the weight finite and >= 0, and the id must not repeat within the token.
+__global__ void __launch_bounds__(1024) plan_kernel(const int *ids, const float *wts, int nt, Plan pl) {
+    __shared__ int cnt[kExperts];
+    __shared__ int run[kExperts];
+    __shared__ unsigned bm[kExperts * (kPlanChunk / 32)];
+    __shared__ int warp_tot[32];
+    __shared__ int s_invalid;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    for (int e = tid; e < kExperts; e += blockDim.x) cnt[e] = 0;
+    if (tid == 0) s_invalid = 0;
+    __syncthreads();
+    // A: validate tokens and count routes per expert.
+    for (int t = tid; t < nt; t += blockDim.x) {
+        bool ok = true;
+        int e_k[kTop];
+#pragma unroll
+        for (int k = 0; k < kTop; k++) {
+            int e = ids[t * kTop + k];
+            float w = wts[t * kTop + k];
+            e_k[k] = e;
+            bool omitted = e <= -2 && e >= -kExperts - 1 && w == 0.0f;
+            if (omitted) {
+                e_k[k] = -1;
+                continue;
+            }
+            if (e < 0 || e >= kExperts || !(w >= 0.0f) || isinf(w)) ok = false;
+#pragma unroll
+            for (int j = 0; j < k; j++)
+                if (ids[t * kTop + j] == e) ok = false;
+        }
+        pl.bad[t] = ok ? 0 : 1;
+        if (ok) {
+#pragma unroll
+            for (int k = 0; k < kTop; k++)
+                if (e_k[k] >= 0) atomicAdd(&cnt[e_k[k]], 1);
+        } else {
+            atomicAdd(&s_invalid, 1);
+        }
+    }
+    __syncthreads();
+    // B: exclusive scan of counts (512 entries, 16 warps of 32).
+    int c = 0, incl = 0;
+    if (tid < kExperts) {
+        c = cnt[tid];
+        incl = c;
+#pragma unroll
+        for (int d = 1; d < 32; d <<= 1) {
+            int v = __shfl_up_sync(0xffffffffu, incl, d);
+            if (lane >= d) incl += v;
+        }
+        if (lane == 31) warp_tot[warp] = incl;
+    }
+    __syncthreads();
+    if (tid < 32) {
+        int v = tid < kExperts / 32 ? warp_tot[tid] : 0, s = v;
+#pragma unroll
+        for (int d = 1; d < 32; d <<= 1) {
+            int o = __shfl_up_sync(0xffffffffu, s, d);
+            if (tid >= d) s += o;
+        }
+        warp_tot[tid] = s - v;  // exclusive prefix of warp totals
+    }
+    __syncthreads();
+    if (tid < kExperts) {
+        int excl = warp_tot[warp] + incl - c;
+        pl.off[tid] = excl;
+        pl.counts[tid] = c;
+        run[tid] = excl;
+        if (tid == kExperts - 1) {
+            pl.off[kExperts] = excl + c;
+            pl.hdr->n_pairs = excl + c;
+        }
+    }
+    // used experts list (ascending): rank = number of used experts below e.
+    __syncthreads();
+    if (tid < kExperts) {
+        unsigned m = __ballot_sync(0xffffffffu, c > 0);
+        if (lane == 0) warp_tot[warp] = __popc(m);
+    }
+    __syncthreads();
+    if (tid < kExperts) {
+        unsigned m = __ballot_sync(0xffffffffu, c > 0);
+        int before = __popc(m & ((1u << lane) - 1));
+        for (int w = 0; w < warp; w++) before += warp_tot[w];
+        if (c > 0) pl.used[before] = tid;
+        if (tid == kExperts - 1) pl.hdr->n_used = before + (c > 0);
+    }
+    if (tid == 0) {
+        pl.hdr->invalid_tokens = s_invalid;
+        pl.hdr->error = 0;
+    }
+    // C: placement, one bitmap chunk of tokens at a time, ascending tokens.
+    constexpr int W = kPlanChunk / 32;
+    for (int c0 = 0; c0 < nt; c0 += kPlanChunk) {
+        __syncthreads();
+        for (int i = tid; i < kExperts * W; i += blockDim.x) bm[i] = 0;
+        __syncthreads();
+        for (int t = c0 + tid; t < min(nt, c0 + kPlanChunk); t += blockDim.x) {
+            if (pl.bad[t]) continue;
+            for (int k = 0; k < kTop; k++) {
+                int e = ids[t * kTop + k];
+                if (e >= 0) atomicOr(&bm[e * W + (t - c0) / 32], 1u << ((t - c0) & 31));
+            }
+        }
+        __syncthreads();
+        for (int e = warp; e < kExperts; e += blockDim.x / 32) {
+            unsigned word = lane < W ? bm[e * W + lane] : 0u;
+            int pc = __popc(word), pre = pc;
+#pragma unroll
+            for (int d = 1; d < 32; d <<= 1) {
+                int v = __shfl_up_sync(0xffffffffu, pre, d);
+                if (lane >= d) pre += v;
+            }
+            int total = __shfl_sync(0xffffffffu, pre, 31);
+            int pos = run[e] + pre - pc;
+            while (word) {
+                int b = __ffs(word) - 1;
+                word &= word - 1;
+                int t = c0 + lane * 32 + b, k = 0;
+                while (k < kTop && ids[t * kTop + k] != e) k++;
+                pl.pairs[pos++] = t * kTop + k;
+            }
+            __syncwarp();
+            if (lane == 0) run[e] += total;
+        }
+    }
+}
+
+// ---------------------------------------------------------------- staging
+// Shared-memory row stride for staged weight rows: padded so consecutive
+// rows start 16 bytes apart modulo 128 (no bank conflicts between the rows
+// a warp reads together).
+__host__ __device__ inline int padded(int bytes) {
+    int r = bytes % 128;
+    return bytes + ((16 - r) + 128) % 128;
+}
+
+// Rows are copied in groups of G consecutive rows so that every TMA bulk copy
+// has a 16-byte-multiple size and a 16-byte-aligned source.
+__host__ __device__ inline int row_group(size_t rb) {
+    int g = 1;
+    while ((g * rb) % 16) g *= 2;
+    return g;
+}
+
+struct Tile {
+    int rb;      // bytes of one row
+    int G;       // rows per bulk copy
+    int gstride; // shared-memory bytes per row group
+    __device__ const unsigned char *row(const unsigned char *base, int r) const {
+        return base + (r / G) * gstride + (r % G) * rb;
+    }
+};
+
+__host__ __device__ inline Tile make_tile(size_t rb) {
+    Tile t;
+    t.rb = (int)rb;
+    t.G = row_group(rb);
+    t.gstride = padded(t.G * (int)rb);
+    return t;
+}
+
+// Issue the bulk copies of `rows` consecutive rows starting at src into dst.
+__device__ inline void tile_load(unsigned char *dst, const unsigned char *src, int rows, const Tile &t,
+                                 uint64_t *bar) {
+    for (int g = 0; g < rows / t.G; g++)
+        tma_load_1d(dst + g * t.gstride, src + (size_t)g * t.G * t.rb, (uint32_t)(t.G * t.rb), bar);
+}
+
+// x staging: each 64-value unit u of a token vector is stored as 32 float2
+// pairs matching the byte layout of the weights, plus the two 32-value
+// group sums (Q4_K min term). The unit stride is padded by 16 bytes.
+constexpr int kUnitFloats = 64 + 4;  // 32 pairs + 2 group sums (+2 pad) = 272 bytes
+
+template <int QT>
+__device__ inline void stage_tokens(float *xs, const float *const *src, int n, int K) {
+    // one warp per (token, unit); lane l writes pair l of that unit
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+    const int units = K / 64;
+    for (int job = warp; job < kTP * units; job += nwarps) {
+        int tp = job / units, u = job % units;
+        float a = 0.0f, b = 0.0f;
+        if (tp < n) {
+            const float *v = src[tp] + u * 64;
+            int ia, ib;
+            if (QT == 12) {
+                ia = lane;
+                ib = lane + 32;
+            } else {  // IQ4_NL: blocks of 32 with byte j holding values j and j+16
+                int blk = lane >> 4, j = lane & 15;
+                ia = blk * 32 + j;
+                ib = blk * 32 + 16 + j;
+            }
+            a = v[ia];
+            b = v[ib];
+        }
+        float *dst = xs + ((size_t)tp * units + u) * kUnitFloats;
+        reinterpret_cast<float2 *>(dst)[lane] = make_float2(a, b);
+        if (QT == 12) {
+            // group sums: values 0..31 (the "a" of every lane) and 32..63 (the "b")
+            float sa = a, sb = b;
+#pragma unroll
+            for (int d = 16; d; d >>= 1) {
+                sa += __shfl_xor_sync(0xffffffffu, sa, d);
+                sb += __shfl_xor_sync(0xffffffffu, sb, d);
+            }
+            if (lane == 0) {
+                dst[64] = sa;
+                dst[65] = sb;
+            }
+        }
+    }
+}
+
+__device__ __forceinline__ float code_f(uint32_t v) { return static_cast<float>(v); }
+
+// Accumulate one 64-value unit u of RM staged rows against the staged
+// tokens: y[rm][tp] += dot(row rm unit u, token tp unit u).
+template <int QT, int RM>
+__device__ inline void unit_dot(const unsigned char *const (&rows)[RM], int u, const float *xs, int units,
+                                const float *lut, float (&y)[RM][kTP]) {
+    if (QT == 12) {
+        const int sb = u >> 2, i = u & 3;
+        float ds_lo[RM], ds_hi[RM], dm_lo[RM], dm_hi[RM];
+        uint4 qa[RM], qb[RM];
+#pragma unroll
+        for (int r = 0; r < RM; r++) {
+            const unsigned char *p = rows[r] + sb * 144;
+            const uint4 h = *reinterpret_cast<const uint4 *>(p);
+            const unsigned char *sc = reinterpret_cast<const unsigned char *>(&h) + 4;
+            int s0, m0, s1, m1;
+            k_scale_min(sc, 2 * i, s0, m0);
+            k_scale_min(sc, 2 * i + 1, s1, m1);
+            float d = half_bits(h.x), dmin = half_bits(h.x >> 16);
+            ds_lo[r] = d * (float)s0;
+            ds_hi[r] = d * (float)s1;
+            dm_lo[r] = dmin * (float)m0;
+            dm_hi[r] = dmin * (float)m1;
+            qa[r] = *reinterpret_cast<const uint4 *>(p + 16 + 32 * i);
+            qb[r] = *reinterpret_cast<const uint4 *>(p + 32 + 32 * i);
+        }
+        float s_lo[RM][kTP], s_hi[RM][kTP];
+#pragma unroll
+        for (int r = 0; r < RM; r++)
+#pragma unroll
+            for (int t = 0; t < kTP; t++) s_lo[r][t] = s_hi[r][t] = 0.0f;
+#pragma unroll
+        for (int w = 0; w < 8; w++) {
+            float2 xv[kTP][4];
+#pragma unroll
+            for (int t = 0; t < kTP; t++) {
+                const float4 *src = reinterpret_cast<const float4 *>(xs + ((size_t)t * units + u) * kUnitFloats) + 2 * w;
+                float4 A = src[0], B = src[1];
+                xv[t][0] = make_float2(A.x, A.y);
+                xv[t][1] = make_float2(A.z, A.w);
+                xv[t][2] = make_float2(B.x, B.y);
+                xv[t][3] = make_float2(B.z, B.w);
+            }
+#pragma unroll
+            for (int r = 0; r < RM; r++) {
+                uint32_t word = w < 4 ? (&qa[r].x)[w] : (&qb[r].x)[w - 4];
+#pragma unroll
+                for (int b = 0; b < 4; b++) {
+                    float ql = code_f((word >> (8 * b)) & 15u), qh = code_f((word >> (8 * b + 4)) & 15u);
+#pragma unroll
+                    for (int t = 0; t < kTP; t++) {
+                        s_lo[r][t] = __fmaf_rn(ql, xv[t][b].x, s_lo[r][t]);
+                        s_hi[r][t] = __fmaf_rn(qh, xv[t][b].y, s_hi[r][t]);
+                    }
+                }
+            }
+        }
+#pragma unroll
+        for (int t = 0; t < kTP; t++) {
+            const float *g = xs + ((size_t)t * units + u) * kUnitFloats + 64;
+            float glo = g[0], ghi = g[1];
+#pragma unroll
+            for (int r = 0; r < RM; r++) {
+                float v = __fmaf_rn(ds_lo[r], s_lo[r][t], ds_hi[r] * s_hi[r][t]);
+                v = __fmaf_rn(-dm_lo[r], glo, v);
+                v = __fmaf_rn(-dm_hi[r], ghi, v);
+                y[r][t] += v;
+            }
+        }
+    } else {  // IQ4_NL: blocks 2u and 2u+1, 36 bytes at offset 36u
+        float dA[RM], dB[RM];
+        uint32_t q[RM][8];
+#pragma unroll
+        for (int r = 0; r < RM; r++) {
+            const uint32_t *p = reinterpret_cast<const uint32_t *>(rows[r] + 36 * u);
+            uint32_t W[9];
+#pragma unroll
+            for (int j = 0; j < 9; j++) W[j] = p[j];
+            dA[r] = half_bits(W[0]);
+            dB[r] = half_bits(W[4] >> 16);
+#pragma unroll
+            for (int j = 0; j < 4; j++) q[r][j] = __byte_perm(W[j], W[j + 1], 0x5432);
+#pragma unroll
+            for (int j = 0; j < 4; j++) q[r][4 + j] = W[5 + j];
+        }
+        float sA[RM][kTP], sB[RM][kTP];
+#pragma unroll
+        for (int r = 0; r < RM; r++)
+#pragma unroll
+            for (int t = 0; t < kTP; t++) sA[r][t] = sB[r][t] = 0.0f;
+#pragma unroll
+        for (int w = 0; w < 8; w++) {
+            float2 xv[kTP][4];
+#pragma unroll
+            for (int t = 0; t < kTP; t++) {
+                const float4 *src = reinterpret_cast<const float4 *>(xs + ((size_t)t * units + u) * kUnitFloats) + 2 * w;
+                float4 A = src[0], B = src[1];
+                xv[t][0] = make_float2(A.x, A.y);
+                xv[t][1] = make_float2(A.z, A.w);
+                xv[t][2] = make_float2(B.x, B.y);
+                xv[t][3] = make_float2(B.z, B.w);
+            }
+#pragma unroll
+            for (int r = 0; r < RM; r++) {
+                uint32_t word = q[r][w];
+#pragma unroll
+                for (int b = 0; b < 4; b++) {
+                    float ql = lut[(word >> (8 * b)) & 15u], qh = lut[(word >> (8 * b + 4)) & 15u];
+#pragma unroll
+                    for (int t = 0; t < kTP; t++) {
+                        float acc = w < 4 ? sA[r][t] : sB[r][t];
+                        acc = __fmaf_rn(ql, xv[t][b].x, acc);
+                        acc = __fmaf_rn(qh, xv[t][b].y, acc);
+                        if (w < 4) sA[r][t] = acc; else sB[r][t] = acc;
+                    }
+                }
+            }
+        }
+#pragma unroll
+        for (int r = 0; r < RM; r++)
+#pragma unroll
+            for (int t = 0; t < kTP; t++) y[r][t] += __fmaf_rn(dA[r], sA[r][t], dB[r] * sB[r][t]);
+    }
+}
+
+__device__ inline void fill_lut(float *lut) {
+    if (threadIdx.x < 16) lut[threadIdx.x] = (float)kIq4nl[threadIdx.x];
+}
+
+// ---------------------------------------------------------------- gate/up
+struct GateUpArgs {
+    const float *x;
+    int nt, H, F;
+    const unsigned char *gate, *up;  // routed experts
+    const unsigned char *sgate, *sup;  // shared expert or null
+    Tile tile;
+    Plan pl;
+    float *mid;  // [(T*10 + T)][F]: pair rows, then shared rows
+    int max_jobs;
+};
+
+template <int QT>
+__global__ void __launch_bounds__(kThreads) gate_up_kernel(GateUpArgs a) {
+    extern __shared__ __align__(128) unsigned char smem[];
+    __shared__ uint64_t bar;
+    __shared__ float lut[16];
+    __shared__ float red[kThreads / 32][kGateUpRows][2][kTP];
+    const int job = blockIdx.y;
+    const bool shared_job = a.sgate && job == a.max_jobs;
+    int e = 0, first = 0, n = 0;
+    if (shared_job) {
+        n = a.nt;
+    } else {
+        if (job >= a.pl.hdr->n_used) return;
+        e = a.pl.used[job];
+        first = a.pl.off[e];
+        n = a.pl.off[e + 1] - first;
+    }
+    const int r0 = blockIdx.x * kGateUpRows;
+    const Tile &tl = a.tile;
+    const int tile_bytes = (kGateUpRows / tl.G) * tl.gstride;
+    unsigned char *sg = smem, *su = smem + tile_bytes;
+    float *xs = reinterpret_cast<float *>(smem + 2 * tile_bytes);
+    const int units = a.H / 64;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        fence_mbar_init();
+    }
+    if (QT == 20) fill_lut(lut);
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const unsigned char *gsrc = (shared_job ? a.sgate : a.gate + (size_t)e * a.F * tl.rb) + (size_t)r0 * tl.rb;
+        const unsigned char *usrc = (shared_job ? a.sup : a.up + (size_t)e * a.F * tl.rb) + (size_t)r0 * tl.rb;
+        mbar_arrive_expect_tx(&bar, 2u * kGateUpRows * tl.rb);
+        tile_load(sg, gsrc, kGateUpRows, tl, &bar);
+        tile_load(su, usrc, kGateUpRows, tl, &bar);
+    }
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int c = lane & 3, rg = lane >> 2;  // 4 unit slots x 8 row pairs per warp
+    const int slot = warp * 4 + c;           // unit slot 0..31
+    const unsigned char *rows[4] = {tl.row(sg, 2 * rg), tl.row(sg, 2 * rg + 1), tl.row(su, 2 * rg),
+                                    tl.row(su, 2 * rg + 1)};
+    bool loaded = false;
+    for (int p0 = 0; p0 < n; p0 += kTP) {
+        const int np = min(kTP, n - p0);
+        const float *src[kTP];
+#pragma unroll
+        for (int t = 0; t < kTP; t++) {
+            int pi = min(t, np - 1);
+            int tok = shared_job ? p0 + pi : a.pl.pairs[first + p0 + pi] / kTop;
+            src[t] = a.x + (size_t)tok * a.H;
+        }
+        __syncthreads();  // previous pass finished reading xs / red
+        stage_tokens<QT>(xs, src, np, a.H);
+        __syncthreads();
+        if (!loaded) {
+            bool ok = mbar_wait_bounded(&bar, 0, &a.pl.hdr->error);
+            if (__syncthreads_or(!ok)) return;  // every thread leaves together on a timeout
+            loaded = true;
+        }
+        float y[4][kTP];
+#pragma unroll
+        for (int r = 0; r < 4; r++)
+#pragma unroll
+            for (int t = 0; t < kTP; t++) y[r][t] = 0.0f;
+        for (int u = slot; u < units; u += 32) unit_dot<QT, 4>(rows, u, xs, units, lut, y);
+        // reduce the 4 unit slots of this warp, then across warps in fixed order
+#pragma unroll
+        for (int r = 0; r < 4; r++)
+#pragma unroll
+            for (int t = 0; t < kTP; t++) {
+                float v = y[r][t];
+                v += __shfl_xor_sync(0xffffffffu, v, 1);
+                v += __shfl_xor_sync(0xffffffffu, v, 2);
+                y[r][t] = v;
+            }
+        if (c == 0) {
+#pragma unroll
+            for (int t = 0; t < kTP; t++) {
+                red[warp][2 * rg][0][t] = y[0][t];
+                red[warp][2 * rg + 1][0][t] = y[1][t];
+                red[warp][2 * rg][1][t] = y[2][t];
+                red[warp][2 * rg + 1][1][t] = y[3][t];
+            }
+        }
+        __syncthreads();
+        if (threadIdx.x < kGateUpRows * kTP) {
+            const int row = threadIdx.x / kTP, t = threadIdx.x % kTP;
+            if (t < np) {
+                float g = 0.0f, uu = 0.0f;
+#pragma unroll
+                for (int w = 0; w < kThreads / 32; w++) {
+                    g += red[w][row][0][t];
+                    uu += red[w][row][1][t];
+                }
+                float m = (g * sigmoidf_ref(g)) * uu;
+                size_t mrow = shared_job ? (size_t)a.nt * kTop + p0 + t : (size_t)(first + p0 + t);
+                a.mid[mrow * a.F + r0 + row] = m;
+            }
+        }
+    }
+}
+
+// ---------------------------------------------------------------- down
+struct DownArgs {
+    int nt, H, F;
+    const unsigned char *down, *sdown;
+    const float *wts;
+    Tile tile;
+    Plan pl;
+    const float *mid;
+    float *slots, *shared;
+    int max_jobs;
+};
+
+template <int QT>
+__global__ void __launch_bounds__(kThreads) down_kernel(DownArgs a) {
+    extern __shared__ __align__(128) unsigned char smem[];
+    __shared__ uint64_t bar;
+    __shared__ float lut[16];
+    const int job = blockIdx.y;
+    const bool shared_job = a.sdown && job == a.max_jobs;
+    int e = 0, first = 0, n = 0;
+    if (shared_job) {
+        n = a.nt;
+    } else {
+        if (job >= a.pl.hdr->n_used) return;
+        e = a.pl.used[job];
+        first = a.pl.off[e];
+        n = a.pl.off[e + 1] - first;
+    }
+    const int r0 = blockIdx.x * kDownRows;
+    const Tile &tl = a.tile;
+    const int tile_bytes = (kDownRows / tl.G) * tl.gstride;
+    unsigned char *sd = smem;
+    float *xs = reinterpret_cast<float *>(smem + tile_bytes);
+    const int units = a.F / 64;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        fence_mbar_init();
+    }
+    if (QT == 20) fill_lut(lut);
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const unsigned char *src = (shared_job ? a.sdown : a.down + (size_t)e * a.H * tl.rb) + (size_t)r0 * tl.rb;
+        mbar_arrive_expect_tx(&bar, (uint32_t)kDownRows * tl.rb);
+        tile_load(sd, src, kDownRows, tl, &bar);
+    }
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int c = lane & 7, rg = warp * 4 + (lane >> 3);  // 8 unit slots x 32 row pairs
+    const unsigned char *rows[2] = {tl.row(sd, 2 * rg), tl.row(sd, 2 * rg + 1)};
+    bool loaded = false;
+    for (int p0 = 0; p0 < n; p0 += kTP) {
+        const int np = min(kTP, n - p0);
+        const float *src[kTP];
+        int slot_of[kTP];
+#pragma unroll
+        for (int t = 0; t < kTP; t++) {
+            int pi = min(t, np - 1);
+            size_t mrow;
+            if (shared_job) {
+                mrow = (size_t)a.nt * kTop + p0 + pi;
+                slot_of[t] = p0 + pi;
+            } else {
+                mrow = (size_t)(first + p0 + pi);
+                slot_of[t] = a.pl.pairs[first + p0 + pi];
+            }
+            src[t] = a.mid + mrow * a.F;
+        }
+        __syncthreads();
+        stage_tokens<QT>(xs, src, np, a.F);
+        __syncthreads();
+        if (!loaded) {
+            bool ok = mbar_wait_bounded(&bar, 0, &a.pl.hdr->error);
+            if (__syncthreads_or(!ok)) return;  // every thread leaves together on a timeout
+            loaded = true;
+        }
+        float y[2][kTP];
+#pragma unroll
+        for (int r = 0; r < 2; r++)
+#pragma unroll
+            for (int t = 0; t < kTP; t++) y[r][t] = 0.0f;
+        for (int u = c; u < units; u += 8) unit_dot<QT, 2>(rows, u, xs, units, lut, y);
+#pragma unroll
+        for (int r = 0; r < 2; r++)
+#pragma unroll
+            for (int t = 0; t < kTP; t++) {
+                float v = y[r][t];
+                v += __shfl_xor_sync(0xffffffffu, v, 1);
+                v += __shfl_xor_sync(0xffffffffu, v, 2);
+                v += __shfl_xor_sync(0xffffffffu, v, 4);
+                y[r][t] = v;
+            }
+        if (c == 0) {
+#pragma unroll
+            for (int t = 0; t < kTP; t++) {
+                if (t >= np) break;
+#pragma unroll
+                for (int r = 0; r < 2; r++) {
+                    int row = r0 + 2 * rg + r;
+                    if (shared_job)
+                        a.shared[(size_t)slot_of[t] * a.H + row] = y[r][t];
+                    else
+                        a.slots[(size_t)slot_of[t] * a.H + row] = y[r][t] * a.wts[slot_of[t]];
+                }
+            }
+        }
+    }
+}
+
+// ---------------------------------------------------------------- combine
+__global__ void combine_kernel(float *out, const float *slots, const int *ids, const float *wts, const int *bad,
+                               const float *shared, const float *sgate, int sgate_stride, int nt, int H) {
+    const int t = blockIdx.y;
+    const int d4 = blockIdx.x * blockDim.x + threadIdx.x;
+    if (d4 * 4 >= H) return;
+    float4 *o = reinterpret_cast<float4 *>(out + (size_t)t * H) + d4;
+    if (bad[t]) {
+        *o = make_float4(NAN, NAN, NAN, NAN);
+        return;
+    }
+    float4 s = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+#pragma unroll
+    for (int k = 0; k < kTop; k++) {
+        float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        if (ids[t * kTop + k] >= 0) v = reinterpret_cast<const float4 *>(slots + ((size_t)t * kTop + k) * H)[d4];
+        s.x += v.x;
+        s.y += v.y;
+        s.z += v.z;
+        s.w += v.w;
+    }
+    if (shared) {
+        float g = sigmoidf_ref(sgate[(size_t)t * sgate_stride]);
+        float4 v = reinterpret_cast<const float4 *>(shared + (size_t)t * H)[d4];
+        s.x = __fmaf_rn(v.x, g, s.x);
+        s.y = __fmaf_rn(v.y, g, s.y);
+        s.z = __fmaf_rn(v.z, g, s.z);
+        s.w = __fmaf_rn(v.w, g, s.w);
+    }
+    *o = s;
+}
+
+// ---------------------------------------------------------------- host side
+bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+struct Shape {
+    int T, H, F;
+};
+
+int check_shape(int T, int H, int F) {
+    if (T < 1 || T > kMaxTokens || H < 64 || F < 64 || H % 64 || F % 64) return cudaErrorInvalidValue;
+    if (F % kGateUpRows || H % kDownRows) return cudaErrorInvalidValue;
+    return 0;
+}
+
+int smem_gate_up(const Tile &t) { return 2 * (kGateUpRows / t.G) * t.gstride; }
+int smem_down(const Tile &t) { return (kDownRows / t.G) * t.gstride; }
+
+template <int QT>
+int launch_gate_up(const GateUpArgs &a, cudaStream_t st) {
+    int bytes = smem_gate_up(a.tile) + kTP * (a.H / 64) * kUnitFloats * 4;
+    int rc = cudaFuncSetAttribute(gate_up_kernel<QT>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (rc) return rc;
+    dim3 grid(a.F / kGateUpRows, a.max_jobs + (a.sgate ? 1 : 0));
+    gate_up_kernel<QT><<<grid, kThreads, bytes, st>>>(a);
+    return cudaGetLastError();
+}
+
+template <int QT>
+int launch_down(const DownArgs &a, cudaStream_t st) {
+    int bytes = smem_down(a.tile) + kTP * (a.F / 64) * kUnitFloats * 4;
+    int rc = cudaFuncSetAttribute(down_kernel<QT>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (rc) return rc;
+    dim3 grid(a.H / kDownRows, a.max_jobs + (a.sdown ? 1 : 0));
+    down_kernel<QT><<<grid, kThreads, bytes, st>>>(a);
+    return cudaGetLastError();
+}
+
+// Routed experts (+ optional shared expert) from device ids/weights.
+int run_experts(float *out, const float *x, const int *ids, const float *wts, int T, const void *gate, int gt,
+                const void *up, int ut, const void *down, int dt, const void *sg, int sgt, const void *su, int sut,
+                const void *sd, int sdt, const float *sgate, int sgate_stride, int H, int F, void *ws,
+                cudaStream_t st) {
+    if (int rc = check_shape(T, H, F)) return rc;
+    if (!out || !x || !ids || !wts || !gate || !up || !down || !ws) return cudaErrorInvalidValue;
+    if (gt != ut || (gt != 12 && gt != 20) || (dt != 12 && dt != 20)) return cudaErrorInvalidValue;
+    size_t grb = row_bytes(gt, H), drb = row_bytes(dt, F);
+    if (!grb || !drb) return cudaErrorInvalidValue;
+    if (!aligned16(gate) || !aligned16(up) || !aligned16(down) || !aligned16(x) || !aligned16(out))
+        return cudaErrorInvalidValue;
+    const bool has_shared = sg != nullptr;
+    if (has_shared) {
+        if (!su || !sd || !sgate || sgt != gt || sut != gt || sdt != dt) return cudaErrorInvalidValue;
+        if (!aligned16(sg) || !aligned16(su) || !aligned16(sd)) return cudaErrorInvalidValue;
+    }
+    Layout L = layout(T, H, F);
+    char *base = static_cast<char *>(ws);
+    if (!aligned16(base)) return cudaErrorInvalidValue;
+    Plan pl = plan_ptrs(ws, L);
+    float *mid = reinterpret_cast<float *>(base + L.mid);
+    float *slots = reinterpret_cast<float *>(base + L.slots);
+    float *shared = reinterpret_cast<float *>(base + L.shared);
+    const int max_jobs = std::min(T * kTop, kExperts);
+
+    {
+        Span sp(kPlan, st);
+        plan_kernel<<<1, 1024, 0, st>>>(ids, wts, T, pl);
+    }
+    if (int rc = cudaGetLastError()) return rc;
+
+    GateUpArgs ga{x, T, H, F, static_cast<const unsigned char *>(gate), static_cast<const unsigned char *>(up),
+                  static_cast<const unsigned char *>(sg), static_cast<const unsigned char *>(su), make_tile(grb),
+                  pl, mid, max_jobs};
+    int rc;
+    {
+        Span sp(kGateUp, st);
+        rc = gt == 12 ? launch_gate_up<12>(ga, st) : launch_gate_up<20>(ga, st);
+    }
+    if (rc) return rc;
+    DownArgs da{T, H, F, static_cast<const unsigned char *>(down), static_cast<const unsigned char *>(sd), wts,
+                make_tile(drb), pl, mid, slots, shared, max_jobs};
+    {
+        Span sp(kDown, st);
+        rc = dt == 12 ? launch_down<12>(da, st) : launch_down<20>(da, st);
+    }
+    if (rc) return rc;
+    {
+        Span sp(kCombine, st);
+        combine_kernel<<<dim3((H / 4 + 127) / 128, T), 128, 0, st>>>(out, slots, ids, wts, pl.bad,
+                                                                    has_shared ? shared : nullptr, sgate,
+                                                                    sgate_stride, T, H);
+    }
+    return cudaGetLastError();
+}
+
+}  // namespace
+
+extern "C" int qg_moe_workspace_bytes(int tokens, int hidden, int ffn, size_t *bytes) {
+    if (!bytes || check_shape(tokens, hidden, ffn)) return cudaErrorInvalidValue;
+    *bytes = layout(tokens, hidden, ffn).total;
+    return 0;
+}
+
+extern "C" int qg_moe_routed(float *out, const float *x, const int *ids, const float *weights, int tokens,
+                             const void *gate, int gt, const void *up, int ut, const void *down, int dt, int hidden,
+                             int ffn, void *workspace) {
+    return run_experts(out, x, ids, weights, tokens, gate, gt, up, ut, down, dt, nullptr, 0, nullptr, 0, nullptr, 0,
+                       nullptr, 0, hidden, ffn, workspace, launch_stream);
+}
+
+extern "C" int qg_moe_layer(float *out, int *ids_out, float *weights_out, const float *x, int tokens,
+                            const float *router, const float *logit_bias, const void *gate, int gt, const void *up, int ut, const void *down,
+                            int dt, const void *sg, int sgt, const void *su, int sut, const void *sd, int sdt,
+                            const float *s_router, int hidden, int ffn, void *workspace) {
+    if (check_shape(tokens, hidden, ffn) || !router || !workspace || (sg && !s_router)) return cudaErrorInvalidValue;
+    cudaStream_t st = launch_stream;
+    Layout L = layout(tokens, hidden, ffn);
+    char *base = static_cast<char *>(workspace);
+    float *logits = reinterpret_cast<float *>(base + L.logits);
+    int *ids = ids_out ? ids_out : reinterpret_cast<int *>(base + L.ids);
+    float *wts = weights_out ? weights_out : reinterpret_cast<float *>(base + L.wts);
+    float *sgate = logits + (size_t)tokens * kExperts;  // [T] shared-gate logits after the router block
+    int rc;
+    {
+        Span sp(kRouter, st);
+        rc = launch_matmul(logits, router, 0, kExperts, hidden, x, tokens, st);
+        if (!rc && sg) rc = launch_matmul(sgate, s_router, 0, 1, hidden, x, tokens, st);
+    }
+    if (rc) return rc;
+    {
+        Span sp(kRoute, st);
+        rc = launch_route(ids, wts, logits, logit_bias, tokens, st);
+    }
+    if (rc) return rc;
+    return run_experts(out, x, ids, wts, tokens, gate, gt, up, ut, down, dt, sg, sgt, su, sut, sd, sdt, sgate, 1,
+                       hidden, ffn, workspace, st);
+}
+
+extern "C" int qg_moe_status(const void *workspace, int *invalid_tokens, int *selected, int *experts) {
+    if (!workspace) return cudaErrorInvalidValue;
+    Header h{};
+    int rc = cudaDeviceSynchronize();
+    if (rc) return rc;
+    if ((rc = cudaMemcpy(&h, workspace, sizeof(h), cudaMemcpyDeviceToHost))) return rc;
+    if (invalid_tokens) *invalid_tokens = h.invalid_tokens;
+    if (selected) *selected = h.n_pairs;
+    if (experts) *experts = h.n_used;
+    return h.error ? cudaErrorLaunchTimeout : 0;
+}
+
+extern "C" int qg_moe_profile(int enable) {
+    g_prof.on = enable != 0;
+    g_prof.spans.clear();
+    g_prof.next = 0;
+    return 0;
+}
+
+extern "C" int qg_moe_profile_read(int phase, double *total_ms, int *launches) {
+    if (phase < 0 || phase >= kPhases || !total_ms || !launches) return cudaErrorInvalidValue;
+    int rc = cudaDeviceSynchronize();
+    if (rc) return rc;
+    double sum = 0;
+    int n = 0;
+    for (auto &sp : g_prof.spans) {
+        if (sp.first != phase) continue;
+        float ms = 0;
+        if ((rc = cudaEventElapsedTime(&ms, sp.second.first, sp.second.second))) return rc;
+        sum += ms;
+        n++;
+    }
+    *total_ms = sum;
+    *launches = n;
+    return 0;
+}
