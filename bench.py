@@ -137,7 +137,7 @@ class Stack:
                 "ids": L.Device.empty((T, K), np.int32), "wts": L.Device.empty((T, K), np.float32),
             }
             self.w.append(d)
-        self.ws = L.Device(nbytes=L.workspace_bytes(T, H, F))
+        self.ws = L.workspace(T, H, F)
 
     def run_layer(self, l: int, x_ptr=None, out_ptr=None):
         d, L = self.w[l], self.L
@@ -359,7 +359,7 @@ def main() -> None:
         dx = L.synth_normal(P * H, 33)
         di, dw = L.Device.empty((P, K), np.int32), L.Device.empty((P, K), np.float32)
         dout = L.Device.empty((P, H), np.float32)
-        pws = L.Device(nbytes=L.workspace_bytes(P, H, F))
+        pws = L.workspace(P, H, F)
         d0 = stack.w[0]
 
         def pre():

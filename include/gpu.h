@@ -103,7 +103,10 @@ int qg_mtp_moe(float *slots, float *mid, const float *x, const int *ids, const f
 /* Device workspace, in bytes, that qg_moe_routed / qg_moe_layer need for a
  * batch of `tokens` at the given shape. Replaces the per-layer host read of
  * route ids (qwen/qwen.c:649) and the per-expert launch loop
- * (qwen/qwen.c:680-698) with device-side grouping. */
+ * (qwen/qwen.c:680-698) with device-side grouping. Fill a new workspace with
+ * zeros once (qg_zero): its counters start at zero and every call returns
+ * them to zero for the next. Calls sharing a workspace must not overlap on
+ * the device. After an error reported by qg_moe_status, zero it again. */
 int qg_moe_workspace_bytes(int tokens, int hidden, int ffn, size_t *bytes);
 
 /* All-resident routed MoE, one call per layer (replaces grouped_moe's GPU

@@ -25,9 +25,11 @@
 // order, so routed outputs match qc_moe within the float tolerance rather
 // than bitwise; the router (ids) and qg_matmul stay bit-exact.
 #include <algorithm>
+#include <cstddef>
 #include <utility>
 #include <vector>
 #include "quant.cuh"
+#include "moe_decode.cuh"
 
 using namespace nb;
 
@@ -88,13 +90,13 @@ inline size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
 
 Layout layout(int T, int H, int F) {
     Layout L{};
-    size_t p = 0;
+    size_t p = kPrefixBytes;  // status words and decode-path counters come first
     auto take = [&](size_t bytes) {
         size_t at = p;
         p = align256(p + bytes);
         return at;
     };
-    L.hdr = take(64);
+    L.hdr = 0;
     L.counts = take(sizeof(int) * kExperts);
     L.off = take(sizeof(int) * (kExperts + 1));
     L.used = take(sizeof(int) * kExperts);
@@ -220,10 +222,7 @@ __global__ void __launch_bounds__(1024) plan_kernel(const int *ids, const float 
         if (c > 0) pl.used[before] = tid;
         if (tid == kExperts - 1) pl.hdr->n_used = before + (c > 0);
     }
-    if (tid == 0) {
-        pl.hdr->invalid_tokens = s_invalid;
-        pl.hdr->error = 0;
-    }
+    if (tid == 0) pl.hdr->invalid_tokens = s_invalid;
     // C: placement, one bitmap chunk of tokens at a time, ascending tokens.
     constexpr int W = kPlanChunk / 32;
     for (int c0 = 0; c0 < nt; c0 += kPlanChunk) {
@@ -827,13 +826,63 @@ int run_experts(float *out, const float *x, const int *ids, const float *wts, in
 
 extern "C" int qg_moe_workspace_bytes(int tokens, int hidden, int ffn, size_t *bytes) {
     if (!bytes || check_shape(tokens, hidden, ffn)) return cudaErrorInvalidValue;
-    *bytes = layout(tokens, hidden, ffn).total;
+    size_t n = layout(tokens, hidden, ffn).total;
+    if (tokens <= kMaxDecodeTokens) n = std::max(n, dec_layout(tokens, hidden, ffn).total);
+    *bytes = n;
     return 0;
 }
+
+namespace {
+// Decode-path arguments over the workspace; ids/wts point at the routing.
+DecArgs dec_args(int T, int H, int F, int gt, int dt, const float *x, float *out, int *ids, float *wts, void *ws) {
+    DecArgs a{};
+    DecLayout L = dec_layout(T, H, F);
+    char *b = static_cast<char *>(ws);
+    a.T = T, a.H = H, a.F = F, a.QG = gt, a.QD = dt;
+    a.x = x;
+    a.out = out;
+    a.ids = ids;
+    a.wts = wts;
+    a.grb = row_bytes(gt, H);
+    a.drb = row_bytes(dt, F);
+    a.hdr = reinterpret_cast<DecHdr *>(b);
+    a.ctr = reinterpret_cast<DecCtr *>(b + kHdrBytes);
+    a.logits = reinterpret_cast<float *>(b + L.logits);
+    a.sgate = reinterpret_cast<float *>(b + L.sgate);
+    a.xpair = reinterpret_cast<float *>(b + L.xpair);
+    a.xsum = reinterpret_cast<float *>(b + L.xsum);
+    a.mid = reinterpret_cast<float *>(b + L.mid);
+    a.msum = reinterpret_cast<float *>(b + L.msum);
+    a.slots = reinterpret_cast<float *>(b + L.slots);
+    a.shout = reinterpret_cast<float *>(b + L.shout);
+    a.off = reinterpret_cast<int *>(b + L.off);
+    a.used = reinterpret_cast<int *>(b + L.used);
+    a.pairs = reinterpret_cast<int *>(b + L.pairs);
+    a.expect = reinterpret_cast<int *>(b + L.expect);
+    return a;
+}
+
+bool dec_pointers_ok(const void *gate, const void *up, const void *down, const float *x, const float *out,
+                     const void *ws) {
+    return aligned16(gate) && aligned16(up) && aligned16(down) && aligned16(x) && aligned16(out) && aligned16(ws);
+}
+}  // namespace
 
 extern "C" int qg_moe_routed(float *out, const float *x, const int *ids, const float *weights, int tokens,
                              const void *gate, int gt, const void *up, int ut, const void *down, int dt, int hidden,
                              int ffn, void *workspace) {
+    if (check_shape(tokens, hidden, ffn) || !out || !x || !ids || !weights || !gate || !up || !down || !workspace)
+        return cudaErrorInvalidValue;
+    if (gt == ut && dec_supported(tokens, hidden, ffn, gt, dt)) {
+        if (!dec_pointers_ok(gate, up, down, x, out, workspace)) return cudaErrorInvalidValue;
+        DecArgs a = dec_args(tokens, hidden, ffn, gt, dt, x, out, const_cast<int *>(ids),
+                             const_cast<float *>(weights), workspace);
+        a.gate = static_cast<const unsigned char *>(gate);
+        a.up = static_cast<const unsigned char *>(up);
+        a.down = static_cast<const unsigned char *>(down);
+        Span sp(kGateUp, launch_stream);
+        return dec_run(a, launch_stream);
+    }
     return run_experts(out, x, ids, weights, tokens, gate, gt, up, ut, down, dt, nullptr, 0, nullptr, 0, nullptr, 0,
                        nullptr, 0, hidden, ffn, workspace, launch_stream);
 }
@@ -844,6 +893,28 @@ extern "C" int qg_moe_layer(float *out, int *ids_out, float *weights_out, const 
                             const float *s_router, int hidden, int ffn, void *workspace) {
     if (check_shape(tokens, hidden, ffn) || !router || !workspace || (sg && !s_router)) return cudaErrorInvalidValue;
     cudaStream_t st = launch_stream;
+    if (gt == ut && dec_supported(tokens, hidden, ffn, gt, dt) && (!sg || (sgt == gt && sut == gt && sdt == dt))) {
+        if (!out || !x || !gate || !up || !down || !dec_pointers_ok(gate, up, down, x, out, workspace) ||
+            !aligned16(router) || (sg && (!su || !sd || !aligned16(sg) || !aligned16(su) || !aligned16(sd) ||
+                                          !aligned16(s_router))))
+            return cudaErrorInvalidValue;
+        DecLayout DL = dec_layout(tokens, hidden, ffn);
+        char *b = static_cast<char *>(workspace);
+        int *ids = ids_out ? ids_out : reinterpret_cast<int *>(b + DL.ids);
+        float *wts = weights_out ? weights_out : reinterpret_cast<float *>(b + DL.wts);
+        DecArgs a = dec_args(tokens, hidden, ffn, gt, dt, x, out, ids, wts, workspace);
+        a.router = router;
+        a.bias = logit_bias;
+        a.s_router = sg ? s_router : nullptr;
+        a.gate = static_cast<const unsigned char *>(gate);
+        a.up = static_cast<const unsigned char *>(up);
+        a.down = static_cast<const unsigned char *>(down);
+        a.sg = static_cast<const unsigned char *>(sg);
+        a.su = static_cast<const unsigned char *>(su);
+        a.sd = static_cast<const unsigned char *>(sd);
+        Span sp(kGateUp, st);
+        return dec_run(a, st);
+    }
     Layout L = layout(tokens, hidden, ffn);
     char *base = static_cast<char *>(workspace);
     float *logits = reinterpret_cast<float *>(base + L.logits);
@@ -872,6 +943,12 @@ extern "C" int qg_moe_status(const void *workspace, int *invalid_tokens, int *se
     int rc = cudaDeviceSynchronize();
     if (rc) return rc;
     if ((rc = cudaMemcpy(&h, workspace, sizeof(h), cudaMemcpyDeviceToHost))) return rc;
+    if (h.error) {  // sticky until read here
+        const int zero = 0;
+        if ((rc = cudaMemcpy(static_cast<char *>(const_cast<void *>(workspace)) + offsetof(Header, error), &zero,
+                             sizeof(zero), cudaMemcpyHostToDevice)))
+            return rc;
+    }
     if (invalid_tokens) *invalid_tokens = h.invalid_tokens;
     if (selected) *selected = h.n_pairs;
     if (experts) *experts = h.n_used;

@@ -1,0 +1,48 @@
+// Interface between the MoE entry points (moe.cu) and the decode kernels
+// (moe_decode.cu), and the fixed workspace prefix both paths share.
+#pragma once
+#include "common.cuh"
+
+namespace nb {
+
+constexpr int kMaxDecodeTokens = 32;
+
+// Workspace prefix: status words, then counters that every call leaves at
+// zero for the next one. The general (large-batch) path never writes here.
+struct DecHdr {
+    int invalid_tokens, n_pairs, n_used, error;
+};
+struct DecCtr {
+    int k1_ticket, queue, k2_ticket, pad[13];
+    int gu_done[kExperts + 1];
+    int tilecnt[kMaxDecodeTokens * 64];
+};
+constexpr size_t kHdrBytes = 256;
+constexpr size_t kPrefixBytes = (kHdrBytes + sizeof(DecCtr) + 255) & ~size_t(255);
+
+struct DecLayout {
+    size_t logits, sgate, ids, wts, xpair, xsum, off, used, pairs, expect, mid, msum, slots, shout, total;
+};
+DecLayout dec_layout(int T, int H, int F);
+
+struct DecArgs {
+    int T, H, F, QG, QD;
+    const float *x;
+    const float *router, *bias, *s_router;  // router == null: ids/wts already hold the routing
+    const unsigned char *gate, *up, *down, *sg, *su, *sd;
+    size_t grb, drb;  // bytes of a gate/up row (hidden values) and of a down row (ffn values)
+    float *out;
+    int *ids;
+    float *wts;
+    DecHdr *hdr;
+    DecCtr *ctr;
+    float *logits, *sgate, *xpair, *xsum, *mid, *msum, *slots, *shout;
+    int *off, *used, *pairs, *expect;
+    // filled by dec_run
+    int gstride, dn_rows, stage_bytes, k1_ctas;
+};
+
+bool dec_supported(int T, int H, int F, int QG, int QD);
+int dec_run(const DecArgs &a, cudaStream_t st);
+
+}  // namespace nb

@@ -135,6 +135,13 @@ def workspace_bytes(tokens: int, hidden: int, ffn: int) -> int:
     return n.value
 
 
+def workspace(tokens: int, hidden: int, ffn: int) -> Device:
+    """A zero-filled MoE workspace (qg_moe_routed / qg_moe_layer need zeros once)."""
+    ws = Device(nbytes=workspace_bytes(tokens, hidden, ffn))
+    call("zero", ws.p, ws.nbytes)
+    return ws
+
+
 def status(ws) -> tuple[int, int, int]:
     """(invalid_tokens, selected pairs, distinct experts) of the last MoE call on ws."""
     a, b, c = I(0), I(0), I(0)

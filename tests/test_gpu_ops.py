@@ -87,7 +87,7 @@ def test_route_matches_restatement(L, restate):
     L.call("route", ids.p, w.p, dl.p, nt)
     rid, rw = restate.route(logits)
     np.testing.assert_array_equal(ids.get(), rid)
-    np.testing.assert_allclose(w.get(), rw, rtol=3e-7, atol=0)
+    np.testing.assert_allclose(w.get(), rw, rtol=1e-6, atol=0)  # CUDA vs host expf: a few ulp
     sel = np.argsort(-logits[4:], axis=1, kind="stable")[:, :10]
     np.testing.assert_array_equal(ids.get()[4:], sel)
     assert (ids.get()[2] == -1).all() and (ids.get()[3] == -1).all()
