@@ -310,7 +310,8 @@ __device__ __forceinline__ uint32_t iq4_lut4(uint32_t q) {
     const uint32_t n = s | (s >> 4);
     const uint32_t sel = __byte_perm(n, 0, 0x0020);
     const uint32_t lo = __byte_perm(T0, T1, sel), hi = __byte_perm(T2, T3, sel);
-    const uint32_t mask = __byte_perm(q << 4, 0, 0xBA98);  // 0xFF where the code is >= 8
+    uint32_t mask;  // 0xFF where the code is >= 8: prmt replicates bit 7 of each byte (selector msb set)
+    asm("prmt.b32 %0, %1, 0, %2;" : "=r"(mask) : "r"(q << 4), "r"(0xBA98u));
     return (hi & mask) | (lo & ~mask);
 }
 // byte b of (lo4, hi4) -> exact code-book values (low nibble, high nibble)
