@@ -83,8 +83,11 @@ constexpr int kPlanChunk = 512;      // tokens per bitmap chunk in the plan kern
 
 // ---------------------------------------------------------------- workspace
 struct Layout {
-    size_t hdr, counts, off, used, pairs, bad, logits, ids, wts, mid, slots, shared, total;
+    size_t hdr, counts, off, used, pairs, bad, logits, ids, wts, mid, slots, shared;
+    size_t x16, xinv, xsum, sub, nsub, mid16, midinv, msum, gudone, tilecnt, expect, total;  // tensor-core path
 };
+
+inline int max_subjobs(int T) { return (T + kTcTok - 1) / kTcTok + kExperts + (T * kTop + kTcTok - 1) / kTcTok; }
 
 inline size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
 
@@ -108,6 +111,17 @@ Layout layout(int T, int H, int F) {
     L.mid = take(sizeof(float) * ((size_t)T * kTop + T) * F);
     L.slots = take(sizeof(float) * (size_t)T * kTop * H);
     L.shared = take(sizeof(float) * (size_t)T * H);
+    L.x16 = take(sizeof(__half) * (size_t)T * 2 * H);
+    L.xinv = take(sizeof(float) * (size_t)T);
+    L.xsum = take(sizeof(float) * (size_t)T * (H / 32));
+    L.sub = take(sizeof(SubJob) * (size_t)max_subjobs(T));
+    L.nsub = take(sizeof(int));
+    L.mid16 = take(sizeof(__half) * ((size_t)T * kTop + T) * 2 * F);
+    L.midinv = take(sizeof(float) * ((size_t)T * kTop + T));
+    L.msum = take(sizeof(float) * ((size_t)T * kTop + T) * (F / 32));
+    L.gudone = take(sizeof(int) * (size_t)max_subjobs(T));
+    L.tilecnt = take(sizeof(int) * (size_t)T * (H / kTcRows));
+    L.expect = take(sizeof(int) * (size_t)T);
     L.total = p;
     return L;
 }
@@ -729,6 +743,67 @@ __global__ void combine_kernel(float *out, const float *slots, const int *ids, c
     *o = s;
 }
 
+// ---------------------------------------------------------------- tensor-core planning
+// Turns the per-expert token lists into token tiles of at most 64 tokens
+// (shared expert first), per-token contribution counts (| bad bit), and
+// zeroes the counters the tensor-core kernel counts up.
+__global__ void __launch_bounds__(1024) tc_plan_kernel(Plan pl, const int *ids, int T, int H, int has_shared,
+                                                      SubJob *sub, int *n_sub, int *expect, int *gu_done,
+                                                      int *tilecnt, float *out) {
+    __shared__ int s_pre[kExperts];
+    __shared__ int s_wt[32];
+    __shared__ int s_total;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int S = has_shared ? (T + kTcTok - 1) / kTcTok : 0;
+    const int n_used = pl.hdr->n_used;
+    for (int i = tid; i < S; i += blockDim.x) sub[i] = SubJob{-1, 0, min(kTcTok, T - i * kTcTok), i * kTcTok};
+    int tiles = 0;
+    if (tid < kExperts && tid < n_used) tiles = (pl.counts[pl.used[tid]] + kTcTok - 1) / kTcTok;
+    int incl = tiles;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+        const int v = __shfl_up_sync(0xffffffffu, incl, d);
+        if (lane >= d) incl += v;
+    }
+    if (lane == 31) s_wt[warp] = incl;
+    __syncthreads();
+    if (tid < 32) {
+        int v = tid < kExperts / 32 ? s_wt[tid] : 0, t = v;
+#pragma unroll
+        for (int d = 1; d < 32; d <<= 1) {
+            const int o = __shfl_up_sync(0xffffffffu, t, d);
+            if (lane >= d) t += o;
+        }
+        s_wt[tid] = t - v;
+        if (tid == 31) s_total = t;
+    }
+    __syncthreads();
+    if (tid < kExperts) s_pre[tid] = s_wt[warp] + incl - tiles;
+    __syncthreads();
+    if (tid < kExperts && tid < n_used) {
+        const int e = pl.used[tid], n = pl.counts[e], first = pl.off[e];
+        for (int i = 0; i < tiles; i++)
+            sub[S + s_pre[tid] + i] = SubJob{e, first + i * kTcTok, min(kTcTok, n - i * kTcTok), 0};
+    }
+    const int total = S + s_total;
+    if (tid == 0) *n_sub = total;
+    for (int i = tid; i < total; i += blockDim.x) gu_done[i] = 0;
+    const int dn_mt = H / kTcRows;
+    for (int i = tid; i < T * dn_mt; i += blockDim.x) tilecnt[i] = 0;
+    for (int t = tid; t < T; t += blockDim.x) {
+        int n = 0;
+        const bool bad = pl.bad[t] != 0;
+        if (!bad)
+            for (int k = 0; k < kTop; k++) n += ids[t * kTop + k] >= 0;
+        const int e = n + has_shared;
+        expect[t] = e | (bad ? 0x10000 : 0);
+        if (e == 0) {
+            const float v = bad ? __int_as_float(0x7fc00000) : 0.0f;
+            for (int d = 0; d < H; d++) out[(size_t)t * H + d] = v;
+        }
+    }
+}
+
 // ---------------------------------------------------------------- host side
 bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
@@ -796,6 +871,48 @@ int run_experts(float *out, const float *x, const int *ids, const float *wts, in
         plan_kernel<<<1, 1024, 0, st>>>(ids, wts, T, pl);
     }
     if (int rc = cudaGetLastError()) return rc;
+    if (tc_supported(H, F, gt, dt)) {
+        // tensor-core path: token tiles, fp16 hi/lo activations, tcgen05 experts
+        TcArgs t{};
+        t.T = T, t.H = H, t.F = F;
+        t.gate = static_cast<const unsigned char *>(gate), t.up = static_cast<const unsigned char *>(up);
+        t.down = static_cast<const unsigned char *>(down);
+        t.sg = static_cast<const unsigned char *>(sg), t.su = static_cast<const unsigned char *>(su);
+        t.sd = static_cast<const unsigned char *>(sd);
+        t.grb = grb, t.drb = drb;
+        t.x16 = reinterpret_cast<__half *>(base + L.x16);
+        t.xinv = reinterpret_cast<float *>(base + L.xinv);
+        t.xsum = reinterpret_cast<float *>(base + L.xsum);
+        t.sub = reinterpret_cast<SubJob *>(base + L.sub);
+        t.n_sub = reinterpret_cast<int *>(base + L.nsub);
+        t.shared_subs = has_shared ? (T + kTcTok - 1) / kTcTok : 0;
+        t.pairs = pl.pairs, t.wts = wts, t.ids = ids;
+        t.expect = reinterpret_cast<int *>(base + L.expect);
+        t.sgate = has_shared ? sgate : nullptr;
+        t.mid = mid, t.mid16 = reinterpret_cast<__half *>(base + L.mid16);
+        t.midinv = reinterpret_cast<float *>(base + L.midinv);
+        t.msum = reinterpret_cast<float *>(base + L.msum);
+        t.slots = slots, t.shout = shared, t.out = out;
+        DecCtr *ctr = reinterpret_cast<DecCtr *>(base + kHdrBytes);
+        t.queue = &ctr->tc_queue, t.tc_ticket = &ctr->tc_ticket;
+        t.gu_done = reinterpret_cast<int *>(base + L.gudone);
+        t.tilecnt = reinterpret_cast<int *>(base + L.tilecnt);
+        t.err = &pl.hdr->error;
+        TcMaps maps;
+        if (int rc = tc_make_maps(t, maps)) return rc;
+        {
+            Span sp(kPlan, st);
+            tc_plan_kernel<<<1, 1024, 0, st>>>(pl, ids, T, H, has_shared ? 1 : 0, const_cast<SubJob *>(t.sub),
+                                               const_cast<int *>(t.n_sub), const_cast<int *>(t.expect), t.gu_done,
+                                               t.tilecnt, out);
+            if (int rc = cudaGetLastError()) return rc;
+            if (int rc = tc_prep_launch(x, T, H, const_cast<__half *>(t.x16), const_cast<float *>(t.xinv),
+                                        const_cast<float *>(t.xsum), st))
+                return rc;
+        }
+        Span sp(kGateUp, st);
+        return tc_launch(t, maps, st, false);
+    }
 
     GateUpArgs ga{x, T, H, F, static_cast<const unsigned char *>(gate), static_cast<const unsigned char *>(up),
                   static_cast<const unsigned char *>(sg), static_cast<const unsigned char *>(su), make_tile(grb),
@@ -859,6 +976,12 @@ DecArgs dec_args(int T, int H, int F, int gt, int dt, const float *x, float *out
     a.used = reinterpret_cast<int *>(b + L.used);
     a.pairs = reinterpret_cast<int *>(b + L.pairs);
     a.expect = reinterpret_cast<int *>(b + L.expect);
+    a.x16 = reinterpret_cast<__half *>(b + L.x16);
+    a.xinv = reinterpret_cast<float *>(b + L.xinv);
+    a.sub = reinterpret_cast<SubJob *>(b + L.sub);
+    a.n_sub = reinterpret_cast<int *>(b + L.nsub);
+    a.mid16 = reinterpret_cast<__half *>(b + L.mid16);
+    a.midinv = reinterpret_cast<float *>(b + L.midinv);
     return a;
 }
 

@@ -152,13 +152,17 @@ __global__ void __launch_bounds__(128) dec_router_kernel(DecArgs a) {
         if ((int)blockIdx.x < T) {
             const int t = blockIdx.x;
             const float *src = xs + (size_t)t * H;
-            float *dst = a.xpair + (size_t)t * H;
-            for (int i = tid; i < H; i += blockDim.x) dst[(i >> 6) * 64 + pair_pos<QG>(i & 63)] = src[i];
-            for (int g = warp; g < H / 32; g += blockDim.x / 32) {
-                float v = src[g * 32 + lane];
+            if (a.use_tc) {
+                tc_prep_token(src, H, a.x16 + (size_t)t * 2 * H, a.xinv + t, a.xsum + (size_t)t * (H / 32));
+            } else {
+                float *dst = a.xpair + (size_t)t * H;
+                for (int i = tid; i < H; i += blockDim.x) dst[(i >> 6) * 64 + pair_pos<QG>(i & 63)] = src[i];
+                for (int g = warp; g < H / 32; g += blockDim.x / 32) {
+                    float v = src[g * 32 + lane];
 #pragma unroll
-                for (int d = 16; d; d >>= 1) v += __shfl_xor_sync(0xffffffffu, v, d);
-                if (lane == 0) a.xsum[t * (H / 32) + g] = v;
+                    for (int d = 16; d; d >>= 1) v += __shfl_xor_sync(0xffffffffu, v, d);
+                    if (lane == 0) a.xsum[t * (H / 32) + g] = v;
+                }
             }
         }
     }
@@ -242,13 +246,17 @@ __global__ void __launch_bounds__(128) dec_router_kernel(DecArgs a) {
             const int e = e0 + j;
             s_off[e] = ot;
             a.off[e] = ot;
-            if (c4[j]) a.used[ou++] = e;
+            if (c4[j]) {
+                if (a.use_tc) a.sub[(a.sg ? 1 : 0) + ou] = SubJob{e, ot, c4[j], 0};
+                a.used[ou++] = e;
+            }
             ot += c4[j];
         }
         if (tid == blockDim.x - 1) {
             a.off[kExperts] = ot;
             a.hdr->n_pairs = ot;
             a.hdr->n_used = ou;
+            if (a.use_tc) *a.n_sub = (a.sg ? 1 : 0) + ou;
         }
     }
     __syncthreads();
@@ -258,6 +266,12 @@ __global__ void __launch_bounds__(128) dec_router_kernel(DecArgs a) {
         a.pairs[s_off[e] + __popc(s_bm[e] & ((1u << t) - 1))] = i;
     }
     const int has_shared = a.sg != nullptr;
+    if (a.use_tc) {
+        // counters the tensor-core kernel counts up from zero
+        for (int i = tid; i <= kExperts; i += blockDim.x) a.ctr->gu_done[i] = 0;
+        for (int i = tid; i < T * (H / kTcRows); i += blockDim.x) a.ctr->tilecnt[i] = 0;
+        if (tid == 0 && has_shared) a.sub[0] = SubJob{-1, 0, T, 0};
+    }
     int invalid = 0;
     for (int t = tid; t < T; t += blockDim.x) {
         int n = 0;
@@ -780,6 +794,12 @@ DecLayout dec_layout(int T, int H, int F) {
     L.msum = take(sizeof(float) * (T * kTop + T) * (F / 32));
     L.slots = take(sizeof(float) * T * kTop * H);
     L.shout = take(sizeof(float) * T * H);
+    L.x16 = take(sizeof(__half) * T * 2 * H);
+    L.xinv = take(sizeof(float) * T);
+    L.sub = take(sizeof(SubJob) * (kExperts + 1));
+    L.nsub = take(sizeof(int));
+    L.mid16 = take(sizeof(__half) * (T * kTop + T) * 2 * F);
+    L.midinv = take(sizeof(float) * (T * kTop + T));
     L.total = p;
     return L;
 }
@@ -802,6 +822,7 @@ bool dec_supported(int T, int H, int F, int QG, int QD) {
 
 int dec_run(const DecArgs &in, cudaStream_t st) {
     DecArgs a = in;
+    a.use_tc = tc_supported(a.H, a.F, a.QG, a.QD) && a.H / kTcRows <= 64;
     const size_t grb = a.grb, drb = a.drb;
     a.gstride = (int)((grb + 127) / 128 * 128 + 16);  // rows start 16 bytes apart modulo 128
     const int gu_bytes = 2 * kGuRows * a.gstride;
@@ -823,6 +844,22 @@ int dec_run(const DecArgs &in, cudaStream_t st) {
     }
 #undef NB_K1
     if (rc) return rc;
+    if (a.use_tc) {
+        TcArgs t{};
+        t.T = a.T, t.H = a.H, t.F = a.F;
+        t.gate = a.gate, t.up = a.up, t.down = a.down, t.sg = a.sg, t.su = a.su, t.sd = a.sd;
+        t.grb = a.grb, t.drb = a.drb;
+        t.x16 = a.x16, t.xinv = a.xinv, t.xsum = a.xsum;
+        t.sub = a.sub, t.n_sub = a.n_sub, t.shared_subs = a.sg ? 1 : 0;
+        t.pairs = a.pairs, t.wts = a.wts, t.ids = a.ids, t.expect = a.expect, t.sgate = a.sg ? a.sgate : nullptr;
+        t.mid = a.mid, t.mid16 = a.mid16, t.midinv = a.midinv, t.msum = a.msum;
+        t.slots = a.slots, t.shout = a.shout, t.out = a.out;
+        t.queue = &a.ctr->tc_queue, t.tc_ticket = &a.ctr->tc_ticket;
+        t.gu_done = a.ctr->gu_done, t.tilecnt = a.ctr->tilecnt, t.err = &a.hdr->error;
+        TcMaps maps;
+        if ((rc = tc_make_maps(t, maps))) return rc;
+        return tc_launch(t, maps, st, true);
+    }
     const int ctas = sm_count();
     if (a.QG == 12 && a.QD == 12) return launch_k2<12, 12>(a, st, ctas);
     if (a.QG == 12 && a.QD == 20) return launch_k2<12, 20>(a, st, ctas);

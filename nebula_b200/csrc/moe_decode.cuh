@@ -2,6 +2,7 @@
 // (moe_decode.cu), and the fixed workspace prefix both paths share.
 #pragma once
 #include "common.cuh"
+#include "moe_tc.cuh"
 
 namespace nb {
 
@@ -13,7 +14,7 @@ struct DecHdr {
     int invalid_tokens, n_pairs, n_used, error;
 };
 struct DecCtr {
-    int k1_ticket, queue, k2_ticket, pad[13];
+    int k1_ticket, queue, k2_ticket, tc_queue, tc_ticket, pad[11];
     int gu_done[kExperts + 1];
     int tilecnt[kMaxDecodeTokens * 64];
 };
@@ -21,7 +22,8 @@ constexpr size_t kHdrBytes = 256;
 constexpr size_t kPrefixBytes = (kHdrBytes + sizeof(DecCtr) + 255) & ~size_t(255);
 
 struct DecLayout {
-    size_t logits, sgate, ids, wts, xpair, xsum, off, used, pairs, expect, mid, msum, slots, shout, total;
+    size_t logits, sgate, ids, wts, xpair, xsum, off, used, pairs, expect, mid, msum, slots, shout;
+    size_t x16, xinv, sub, nsub, mid16, midinv, total;  // tensor-core path
 };
 DecLayout dec_layout(int T, int H, int F);
 
@@ -38,6 +40,12 @@ struct DecArgs {
     DecCtr *ctr;
     float *logits, *sgate, *xpair, *xsum, *mid, *msum, *slots, *shout;
     int *off, *used, *pairs, *expect;
+    // tensor-core path (Q4_K): fp16 hi/lo activations and sub-jobs
+    int use_tc;
+    __half *x16, *mid16;
+    float *xinv, *midinv;
+    SubJob *sub;
+    int *n_sub;
     // filled by dec_run
     int gstride, dn_rows, stage_bytes, k1_ctas;
 };
