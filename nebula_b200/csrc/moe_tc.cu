@@ -348,6 +348,9 @@ __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a,
         // ------------------------------------------------------ converters
         const int ct = tid - kConvWarp0 * 32;  // weight row of the tile
         int gsb = 0, gch = 0;
+        // activations, routing and plan come from the preceding kernel: wait for it
+        // (only the producer's weight prefetch may run ahead of it)
+        grid_dep_wait();
         for (int seq = 0;; seq++) {
             const int slot = seq & 3;
             if (!wait_phase(&bars.item_full[slot], (seq >> 2) & 1, &abort_flag, err)) break;
@@ -421,6 +424,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a,
         const int half = ew >> 2;                // token half
         const int et = tid - kEpiWarp0 * 32;     // 0..255
         int gsb = 0;
+        grid_dep_wait();  // scales, group sums and routing from the preceding kernel
         for (int seq = 0;; seq++) {
             const int slot = seq & 3;
             if (!wait_phase(&bars.item_full[slot], (seq >> 2) & 1, &abort_flag, err)) break;
