@@ -43,7 +43,8 @@ constexpr int kSbBytes = kTcRows * 144;          // one superblock of 128 Q4_K r
 constexpr int kRawStage = 2 * kSbBytes;          // gate + up
 constexpr int kABytes = kTcRows * 64 * 2;        // 128 rows x 64 halves
 constexpr int kBBytes = 2 * kTcTok * 64 * 2;     // up to 128 B rows x 64 halves
-constexpr int kScSlot = 2 * kTcRows * 16;        // d, dmin, m[8] per row per matrix
+constexpr int kScRows = 2 * kTcRows * 16;        // d, dmin, m[8] per row per matrix
+constexpr int kScSlot = kScRows + 8 * kTcTok * 4; // + the superblock's 8 group sums per token
 constexpr int kOffRaw = 0, kOffA = kOffRaw + 2 * kRawStage, kOffB = kOffA + 2 * 2 * kABytes,
               kOffSc = kOffB + 2 * kBBytes, kSmem = kOffSc + 4 * kScSlot;
 constexpr uint32_t kBad = 1u << 16;
@@ -202,10 +203,28 @@ __device__ __forceinline__ uint4 q4k_row_scales(const unsigned char *row) {
     return make_uint4(__float_as_uint(d), __float_as_uint(dmin), m4[0], m4[1]);
 }
 
+// Per-item token table, filled once per item (shared by all roles).
+struct __align__(16) TokTab {
+    int tok[kTcTok];   // token index
+    int src[kTcTok];   // B source row, in halves: x16 row (gate/up) or mid16 row (down)
+    int mrow[kTcTok];  // mid row written (gate/up) or read (down)
+    int slot[kTcTok];  // routed slot t*10+k (down)
+    float w[kTcTok];   // route weight (down)
+    float inv[kTcTok]; // 1/s of the B row (filled by the converters)
+};
+
+__device__ __forceinline__ void tmem_ld8_nw(uint32_t addr, uint32_t (&r)[8]) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+                 : "r"(addr));
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
 __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a, const __grid_constant__ TcMaps maps) {
     extern __shared__ __align__(1024) unsigned char smem[];
     __shared__ Bars bars;
     __shared__ Item items[4];
+    __shared__ TokTab tabs[4];
     __shared__ uint32_t tmem_base;
     __shared__ volatile int abort_flag;
     __shared__ int s_flag;
@@ -246,62 +265,82 @@ __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a,
     int *err = a.err;
 
     if (warp == 0) {
-        // ------------------------------------------------------ producer
-        if (lane == 0) {
-            bool planned = false;
-            int nsub = a.shared_subs;
-            int gsb = 0;
-            const int S_gu = a.shared_subs * gu_mt;
-            for (int seq = 0;; seq++) {
-                const int slot = seq & 3;
-                if (seq >= 4 && !wait_phase(&bars.item_empty[slot], ((seq >> 2) - 1) & 1, &abort_flag, err)) break;
-                const int idx = abort_flag ? 1 << 30 : atomicAdd(a.queue, 1);
-                if (idx >= S_gu && !planned) {
+        // ------------------------------------------------------ producer warp
+        bool planned = false;
+        int nsub = a.shared_subs;
+        int gsb = 0;
+        const int S_gu = a.shared_subs * gu_mt;
+        for (int seq = 0;; seq++) {
+            const int slot = seq & 3;
+            int idx = 1 << 30;
+            if (lane == 0) {
+                bool ok = seq < 4 || wait_phase(&bars.item_empty[slot], ((seq >> 2) - 1) & 1, &abort_flag, err);
+                if (ok && !abort_flag) idx = atomicAdd(a.queue, 1);
+                if (idx >= S_gu && idx != (1 << 30) && !planned) {
                     grid_dep_wait();
                     nsub = __ldcg(a.n_sub);
                     planned = true;
                 }
-                Item it{kEnd, 0, 0, -1, 0, 0, 0};
-                const int total_gu = nsub * gu_mt, total_dn = nsub * dn_mt;
-                if (idx < total_gu) {
-                    it.kind = kGU, it.sub = idx / gu_mt, it.mt = idx % gu_mt;
-                } else if (idx < total_gu + total_dn) {
-                    it.kind = kDN, it.sub = (idx - total_gu) / dn_mt, it.mt = (idx - total_gu) % dn_mt;
+            }
+            idx = __shfl_sync(0xffffffffu, idx, 0);
+            nsub = __shfl_sync(0xffffffffu, nsub, 0);
+            if (idx >= S_gu && idx != (1 << 30)) grid_dep_wait();
+            Item it{kEnd, 0, 0, -1, 0, 0, 0};
+            const int total_gu = nsub * gu_mt, total_dn = nsub * dn_mt;
+            if (idx < total_gu) {
+                it.kind = kGU, it.sub = idx / gu_mt, it.mt = idx % gu_mt;
+            } else if (idx < total_gu + total_dn) {
+                it.kind = kDN, it.sub = (idx - total_gu) / dn_mt, it.mt = (idx - total_gu) % dn_mt;
+            }
+            if (it.kind != kEnd) {
+                if (it.sub < a.shared_subs) {  // known without the routing
+                    it.expert = -1, it.tok0 = it.sub * kTcTok, it.n = min(kTcTok, T - it.tok0), it.first = 0;
+                } else {
+                    it.expert = __ldcg(&a.sub[it.sub].expert);
+                    it.first = __ldcg(&a.sub[it.sub].first);
+                    it.n = __ldcg(&a.sub[it.sub].n);
                 }
-                if (it.kind != kEnd) {
-                    if (it.sub < a.shared_subs) {  // known without the routing
-                        it.expert = -1, it.tok0 = it.sub * kTcTok, it.n = min(kTcTok, T - it.tok0), it.first = 0;
-                    } else {
-                        it.expert = __ldcg(&a.sub[it.sub].expert);
-                        it.first = __ldcg(&a.sub[it.sub].first);
-                        it.n = __ldcg(&a.sub[it.sub].n);
-                        it.tok0 = 0;
-                    }
+                TokTab &tb = tabs[slot];
+                for (int j = lane; j < it.n; j += 32) {
+                    const bool sh = it.expert < 0;
+                    const int sl = sh ? 0 : __ldcg(a.pairs + it.first + j);
+                    const int tok = sh ? it.tok0 + j : sl / kTop;
+                    const int mrow = sh ? T * kTop + it.tok0 + j : it.first + j;
+                    tb.tok[j] = tok;
+                    tb.mrow[j] = mrow;
+                    tb.src[j] = it.kind == kGU ? tok * 2 * H : mrow * 2 * F;
+                    tb.slot[j] = sl;
+                    tb.w[j] = (sh || it.kind == kGU) ? 0.0f : __ldcg(a.wts + sl);
                 }
+            }
+            __syncwarp();
+            if (lane == 0) {
                 items[slot] = it;
                 arrive(&bars.item_full[slot]);
-                if (it.kind == kEnd) break;
-                const int nsb = it.kind == kGU ? gu_sb : dn_sb;
-                for (int sb = 0; sb < nsb; sb++, gsb++) {
-                    const int st = gsb & 1;
-                    if (gsb >= 2 && !wait_phase(&bars.raw_empty[st], ((gsb >> 1) - 1) & 1, &abort_flag, err)) break;
-                    unsigned char *dst = smem + kOffRaw + st * kRawStage;
-                    if (it.kind == kGU) {
-                        const int y = (it.expert < 0 ? 0 : it.expert * F) + it.mt * kTcRows;
-                        mbar_arrive_expect_tx(&bars.raw_full[st], 2 * kSbBytes);
-                        tma_2d(dst, it.expert < 0 ? &maps.sg : &maps.gate, sb * 144, y, &bars.raw_full[st]);
-                        tma_2d(dst + kSbBytes, it.expert < 0 ? &maps.su : &maps.up, sb * 144, y, &bars.raw_full[st]);
-                    } else {
-                        const int y = (it.expert < 0 ? 0 : it.expert * H) + it.mt * kTcRows;
-                        mbar_arrive_expect_tx(&bars.raw_full[st], kSbBytes);
-                        tma_2d(dst, it.expert < 0 ? &maps.sd : &maps.down, sb * 144, y, &bars.raw_full[st]);
+                if (it.kind != kEnd) {
+                    const int nsb = it.kind == kGU ? gu_sb : dn_sb;
+                    for (int sb = 0; sb < nsb; sb++, gsb++) {
+                        const int st = gsb & 1;
+                        if (gsb >= 2 && !wait_phase(&bars.raw_empty[st], ((gsb >> 1) - 1) & 1, &abort_flag, err)) break;
+                        unsigned char *dst = smem + kOffRaw + st * kRawStage;
+                        if (it.kind == kGU) {
+                            const int y = (it.expert < 0 ? 0 : it.expert * F) + it.mt * kTcRows;
+                            mbar_arrive_expect_tx(&bars.raw_full[st], 2 * kSbBytes);
+                            tma_2d(dst, it.expert < 0 ? &maps.sg : &maps.gate, sb * 144, y, &bars.raw_full[st]);
+                            tma_2d(dst + kSbBytes, it.expert < 0 ? &maps.su : &maps.up, sb * 144, y, &bars.raw_full[st]);
+                        } else {
+                            const int y = (it.expert < 0 ? 0 : it.expert * H) + it.mt * kTcRows;
+                            mbar_arrive_expect_tx(&bars.raw_full[st], kSbBytes);
+                            tma_2d(dst, it.expert < 0 ? &maps.sd : &maps.down, sb * 144, y, &bars.raw_full[st]);
+                        }
                     }
                 }
-                if (abort_flag) break;
             }
-            // drain: the last copies this producer issued have landed before the CTA can exit
-            for (int k = max(0, gsb - 2); k < gsb; k++) wait_drain(&bars.raw_full[k & 1], (k >> 1) & 1);
+            __syncwarp();
+            if (it.kind == kEnd || abort_flag) break;
         }
+        if (lane == 0)  // the last copies issued have landed before the CTA may exit
+            for (int k = max(0, gsb - 2); k < gsb; k++) wait_drain(&bars.raw_full[k & 1], (k >> 1) & 1);
     } else if (warp == 1) {
         // ------------------------------------------------------ MMA issuer
         if (lane == 0) {
@@ -328,8 +367,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a,
                         for (int s = 0; s < 4; s++) {
                             const uint64_t bd = umma_desc(b_base + ab * kBBytes + 2 * s * 128, 128, 1024);
                             for (int m = 0; m < mats; m++) {
-                                const uint64_t ad =
-                                    umma_desc(a_base + (ab * 2 + m) * kABytes + 2 * s * 128, 128, 1024);
+                                const uint64_t ad = umma_desc(a_base + (ab * 2 + m) * kABytes + 2 * s * 128, 128, 1024);
                                 mma_f16(tmem + (uint32_t)((db * 2 + m) * 128), ad, bd, idesc, (c | s) != 0);
                             }
                         }
@@ -346,24 +384,31 @@ __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a,
         }
     } else if (warp < kEpiWarp0) {
         // ------------------------------------------------------ converters
+        grid_dep_wait();  // activations, routing and plan come from the preceding kernel
         const int ct = tid - kConvWarp0 * 32;  // weight row of the tile
         int gsb = 0, gch = 0;
-        // activations, routing and plan come from the preceding kernel: wait for it
-        // (only the producer's weight prefetch may run ahead of it)
-        grid_dep_wait();
         for (int seq = 0;; seq++) {
             const int slot = seq & 3;
             if (!wait_phase(&bars.item_full[slot], (seq >> 2) & 1, &abort_flag, err)) break;
             const Item it = items[slot];
             if (it.kind == kEnd) break;
+            TokTab &tb = tabs[slot];
             const int n_pad = (it.n + 15) & ~15, N = 2 * n_pad;
             const int mats = it.kind == kGU ? 2 : 1;
             const int nsb = it.kind == kGU ? gu_sb : dn_sb;
+            const int K = it.kind == kGU ? H : F;
+            const int ngroups = K / 32;
+            const __half *bsrc = it.kind == kGU ? a.x16 : a.mid16;
+            const float *gsums = it.kind == kGU ? a.xsum : a.msum;
             if (it.kind == kDN) {
                 // the token tile's mid must be complete and converted (gu_done = gu_mt + 1)
                 if (ct == 0 && !wait_geq_int(a.gu_done + it.sub, gu_mt + 1, err)) abort_flag = 1;
                 bar_named(2, 128);
             }
+            if (ct < kTcTok)  // padding tokens get 0 so their (discarded) columns stay finite
+                tb.inv[ct] = ct >= it.n ? 0.0f : it.kind == kGU ? __ldcg(a.xinv + tb.tok[ct]) : __ldcg(a.midinv + tb.mrow[ct]);
+            const int grow = ct < it.n ? (it.kind == kGU ? tb.tok[ct] : tb.mrow[ct]) : 0;  // group-sum row
+            bar_named(2, 128);
             bool ok = !abort_flag;
             for (int sb = 0; sb < nsb && ok; sb++, gsb++) {
                 const int st = gsb & 1, sc_slot = gsb & 3;
@@ -371,34 +416,39 @@ __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a,
                 const unsigned char *raw = smem + kOffRaw + st * kRawStage;
                 if (gsb >= 4 && !(ok = wait_phase(&bars.sc_empty[sc_slot], ((gsb >> 2) - 1) & 1, &abort_flag, err)))
                     break;
-                uint4 *scs = reinterpret_cast<uint4 *>(smem + kOffSc + sc_slot * kScSlot);
+                unsigned char *scb = smem + kOffSc + sc_slot * kScSlot;
+                uint4 *scs = reinterpret_cast<uint4 *>(scb);
+                float *xs = reinterpret_cast<float *>(scb + kScRows);  // [8][64]
                 for (int m = 0; m < mats; m++) scs[m * kTcRows + ct] = q4k_row_scales(raw + m * kSbBytes + ct * 144);
+                if (ct < kTcTok) {
+                    float4 v0 = make_float4(0.f, 0.f, 0.f, 0.f), v1 = v0;
+                    if (ct < it.n) {
+                        const float4 *gp = reinterpret_cast<const float4 *>(gsums + (size_t)grow * ngroups + sb * 8);
+                        v0 = __ldcg(gp);
+                        v1 = __ldcg(gp + 1);
+                    }
+                    xs[0 * kTcTok + ct] = v0.x, xs[1 * kTcTok + ct] = v0.y, xs[2 * kTcTok + ct] = v0.z;
+                    xs[3 * kTcTok + ct] = v0.w, xs[4 * kTcTok + ct] = v1.x, xs[5 * kTcTok + ct] = v1.y;
+                    xs[6 * kTcTok + ct] = v1.z, xs[7 * kTcTok + ct] = v1.w;
+                }
                 __syncwarp();
                 if (lane == 0) arrive(&bars.sc_full[sc_slot]);
                 for (int c = 0; c < 4; c++, gch++) {
                     const int ab = gch & 1;
                     if (gch >= 2 && !(ok = wait_phase(&bars.ab_empty[ab], ((gch >> 1) - 1) & 1, &abort_flag, err)))
                         break;
-                    // B rows: token j hi -> row j, lo -> row n_pad + j; k-slots = values 64u .. 64u+63
+                    // B rows: token j hi -> row j, lo -> row n_pad + j; k-slots = values 64u .. 64u+63.
+                    // Eight consecutive threads fill the eight rows of one core matrix (128 B).
                     const int u = sb * 4 + c;
                     unsigned char *bt = smem + kOffB + ab * kBBytes;
                     for (int sgi = ct; sgi < N * 8; sgi += 128) {
-                        const int row = sgi >> 3, kb = sgi & 7;
+                        const int rr = sgi & 7, kb = (sgi >> 3) & 7, row = (sgi >> 6) * 8 + rr;
                         const int j = row < n_pad ? row : row - n_pad, hl = row < n_pad ? 0 : 1;
-                        unsigned char *dst = bt + ((row >> 3) * 8 + kb) * 128 + (row & 7) * 16;
-                        if (j < it.n) {
-                            const __half *src;
-                            if (it.kind == kGU) {
-                                const int tok = it.expert < 0 ? it.tok0 + j : __ldcg(a.pairs + it.first + j) / kTop;
-                                src = a.x16 + ((size_t)tok * 2 + hl) * H;
-                            } else {
-                                const size_t mrow = it.expert < 0 ? (size_t)T * kTop + it.tok0 + j : (size_t)(it.first + j);
-                                src = a.mid16 + (mrow * 2 + hl) * F;
-                            }
-                            cp_async16(dst, src + u * 64 + kb * 8);
-                        } else {
+                        unsigned char *dst = bt + ((row >> 3) * 8 + kb) * 128 + rr * 16;
+                        if (j < it.n)
+                            cp_async16(dst, bsrc + (size_t)tb.src[j] + hl * K + u * 64 + kb * 8);
+                        else
                             *reinterpret_cast<uint4 *>(dst) = make_uint4(0, 0, 0, 0);
-                        }
                     }
                     for (int m = 0; m < mats; m++) {
                         unsigned char *at = smem + kOffA + (ab * 2 + m) * kABytes + ((ct >> 3) * 8) * 128 + (ct & 7) * 16;
@@ -418,41 +468,43 @@ __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a,
         }
     } else {
         // ------------------------------------------------------ epilogue
+        grid_dep_wait();
         const int ew = warp - kEpiWarp0;         // 0..7
         const int q = warp & 3;                  // TMEM lane quarter
         const int r = 32 * q + lane;             // row within the tile
         const int half = ew >> 2;                // token half
         const int et = tid - kEpiWarp0 * 32;     // 0..255
         int gsb = 0;
-        grid_dep_wait();  // scales, group sums and routing from the preceding kernel
         for (int seq = 0;; seq++) {
             const int slot = seq & 3;
             if (!wait_phase(&bars.item_full[slot], (seq >> 2) & 1, &abort_flag, err)) break;
             const Item it = items[slot];
             if (it.kind == kEnd) break;
+            const TokTab &tb = tabs[slot];
             const int n_pad = (it.n + 15) & ~15, hw = n_pad >> 1;  // tokens per half (multiple of 8)
             const int j0 = half * hw;
             const int mats = it.kind == kGU ? 2 : 1;
             const int nsb = it.kind == kGU ? gu_sb : dn_sb;
-            const int ngroups = (it.kind == kGU ? H : F) / 32;
-            // per-token bases: scale inverse and group sums
-            float acc[2][32];
+            float2 acc[2][16];
 #pragma unroll
             for (int m = 0; m < 2; m++)
 #pragma unroll
-                for (int j = 0; j < 32; j++) acc[m][j] = 0.0f;
+                for (int p = 0; p < 16; p++) acc[m][p] = make_float2(0.0f, 0.0f);
             bool ok = true;
             for (int sb = 0; sb < nsb && ok; sb++, gsb++) {
                 const int db = gsb & 1, sc_slot = gsb & 3;
                 if (!(ok = wait_phase(&bars.d_full[db], (gsb >> 1) & 1, &abort_flag, err))) break;
                 if (!(ok = wait_phase(&bars.sc_full[sc_slot], (gsb >> 2) & 1, &abort_flag, err))) break;
                 tc_fence_after();
-                const uint4 *scs = reinterpret_cast<const uint4 *>(smem + kOffSc + sc_slot * kScSlot);
+                const unsigned char *scb = smem + kOffSc + sc_slot * kScSlot;
+                const uint4 *scs = reinterpret_cast<const uint4 *>(scb);
+                const float *xs = reinterpret_cast<const float *>(scb + kScRows);
 #pragma unroll
                 for (int m = 0; m < 2; m++) {
                     if (m >= mats) break;
                     const uint4 sv = scs[m * kTcRows + r];
-                    const float d = __uint_as_float(sv.x), dmin = __uint_as_float(sv.y);
+                    const float2 d2 = make_float2(__uint_as_float(sv.x), __uint_as_float(sv.x));
+                    const float2 nm2 = make_float2(-__uint_as_float(sv.y), -__uint_as_float(sv.y));
                     float mg[8];
 #pragma unroll
                     for (int g = 0; g < 8; g++) mg[g] = (float)(((g < 4 ? sv.z : sv.w) >> (8 * (g & 3))) & 0xFFu);
@@ -460,29 +512,24 @@ __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a,
 #pragma unroll
                     for (int cb = 0; cb < 4; cb++) {
                         if (cb * 8 >= hw) break;
-                        float vh[8], vl[8];
-                        tmem_ld8(col0 + j0 + cb * 8, vh);
-                        tmem_ld8(col0 + n_pad + j0 + cb * 8, vl);
+                        uint32_t rh[8], rl[8];
+                        tmem_ld8_nw(col0 + j0 + cb * 8, rh);
+                        tmem_ld8_nw(col0 + n_pad + j0 + cb * 8, rl);
+                        tmem_wait_ld();
 #pragma unroll
-                        for (int jj = 0; jj < 8; jj++) {
-                            const int j = j0 + cb * 8 + jj;
-                            if (j >= it.n) continue;
-                            float inv;
-                            const float *gsum;
-                            if (it.kind == kGU) {
-                                const int tok = it.expert < 0 ? it.tok0 + j : __ldcg(a.pairs + it.first + j) / kTop;
-                                inv = __ldcg(a.xinv + tok);
-                                gsum = a.xsum + (size_t)tok * ngroups + sb * 8;
-                            } else {
-                                const size_t row = it.expert < 0 ? (size_t)T * kTop + it.tok0 + j : (size_t)(it.first + j);
-                                inv = __ldcg(a.midinv + row);
-                                gsum = a.msum + row * ngroups + sb * 8;
-                            }
-                            float mterm = 0.0f;
+                        for (int pp = 0; pp < 4; pp++) {
+                            const int j = j0 + cb * 8 + 2 * pp;
+                            const float2 hi = make_float2(__uint_as_float(rh[2 * pp]), __uint_as_float(rh[2 * pp + 1]));
+                            const float2 lo = make_float2(__uint_as_float(rl[2 * pp]), __uint_as_float(rl[2 * pp + 1]));
+                            const float2 inv = *reinterpret_cast<const float2 *>(&tb.inv[j]);
+                            const float2 dot = __fmul2_rn(__ffma2_rn(lo, make_float2(1.0f / 2048.0f, 1.0f / 2048.0f), hi), inv);
+                            float2 mt = make_float2(0.0f, 0.0f);
 #pragma unroll
-                            for (int g = 0; g < 8; g++) mterm = __fmaf_rn(mg[g], __ldcg(gsum + g), mterm);
-                            const float dot = __fmaf_rn(vl[jj], 1.0f / 2048.0f, vh[jj]) * inv;
-                            acc[m][cb * 8 + jj] = __fmaf_rn(d, dot, __fmaf_rn(-dmin, mterm, acc[m][cb * 8 + jj]));
+                            for (int g = 0; g < 8; g++)
+                                mt = __ffma2_rn(make_float2(mg[g], mg[g]), *reinterpret_cast<const float2 *>(&xs[g * kTcTok + j]), mt);
+                            float2 &ac = acc[m][cb * 4 + pp];
+                            ac = __ffma2_rn(d2, dot, ac);
+                            ac = __ffma2_rn(nm2, mt, ac);
                         }
                     }
                 }
@@ -495,22 +542,26 @@ __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a,
             }
             if (ok) {
                 if (it.kind == kGU) {
-                    for (int jj = 0; jj < hw && j0 + jj < it.n; jj++) {
-                        const int j = j0 + jj;
-                        const float g = acc[0][jj], uu = acc[1][jj];
-                        const float mval = (g * sigmoidf_ref(g)) * uu;
-                        const size_t mrow = it.expert < 0 ? (size_t)T * kTop + it.tok0 + j : (size_t)(it.first + j);
-                        a.mid[mrow * F + it.mt * kTcRows + r] = mval;
+#pragma unroll
+                    for (int p = 0; p < 16; p++) {
+#pragma unroll
+                        for (int e = 0; e < 2; e++) {
+                            const int jj = 2 * p + e, j = j0 + jj;
+                            if (jj < hw && j < it.n) {
+                                const float g = e ? acc[0][p].y : acc[0][p].x, uu = e ? acc[1][p].y : acc[1][p].x;
+                                a.mid[(size_t)tb.mrow[j] * F + it.mt * kTcRows + r] = (g * sigmoidf_ref(g)) * uu;
+                            }
+                        }
                     }
                     __threadfence();
                     bar_named(3, 256);
                     if (et == 0) s_flag = atomicAdd(a.gu_done + it.sub, 1) == gu_mt - 1;
                     bar_named(3, 256);
                     if (s_flag) {
-                        // last gate/up tile of this token tile: convert its mid rows for the down tiles
+                        // last gate/up tile of this token tile: fp16 hi/lo copies of its mid rows
                         __threadfence();
                         for (int j = ew; j < it.n; j += 8) {
-                            const size_t mrow = it.expert < 0 ? (size_t)T * kTop + it.tok0 + j : (size_t)(it.first + j);
+                            const size_t mrow = (size_t)tb.mrow[j];
                             const float *src = a.mid + mrow * F;
                             float mx = 0.0f;
                             for (int i = lane; i < F; i += 32) mx = fmaxf(mx, fabsf(__ldcg(src + i)));
@@ -539,14 +590,17 @@ __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a,
                         if (et == 0) atomicAdd(a.gu_done + it.sub, 1);
                     }
                 } else {
-                    for (int jj = 0; jj < hw && j0 + jj < it.n; jj++) {
-                        const int j = j0 + jj;
-                        const int row = it.mt * kTcRows + r;
-                        if (it.expert < 0) {
-                            a.shout[(size_t)(it.tok0 + j) * H + row] = acc[0][jj];
-                        } else {
-                            const int sl = __ldcg(a.pairs + it.first + j);
-                            a.slots[(size_t)sl * H + row] = acc[0][jj] * __ldcg(a.wts + sl);
+                    const int row = it.mt * kTcRows + r;
+#pragma unroll
+                    for (int p = 0; p < 16; p++) {
+#pragma unroll
+                        for (int e = 0; e < 2; e++) {
+                            const int jj = 2 * p + e, j = j0 + jj;
+                            if (jj < hw && j < it.n) {
+                                const float y = e ? acc[0][p].y : acc[0][p].x;
+                                if (it.expert < 0) a.shout[(size_t)tb.tok[j] * H + row] = y;
+                                else a.slots[(size_t)tb.slot[j] * H + row] = y * tb.w[j];
+                            }
                         }
                     }
                     __threadfence();
@@ -554,7 +608,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a,
                     if (et == 0) s_ncombine = 0;
                     bar_named(3, 256);
                     if (et < it.n) {
-                        const int t = it.expert < 0 ? it.tok0 + et : __ldcg(a.pairs + it.first + et) / kTop;
+                        const int t = tb.tok[et];
                         int *cnt = a.tilecnt + (size_t)t * dn_mt + it.mt;
                         const int expect = __ldcg(a.expect + t) & 0xffff;
                         if (atomicAdd(cnt, 1) == expect - 1) {
@@ -568,17 +622,16 @@ __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a,
                         __threadfence();
                         for (int ci = et >> 7; ci < nc; ci += 2) {
                             const int t = s_combine[ci];
-                            const int rr = et & 127;
-                            const int row = it.mt * kTcRows + rr;
+                            const int rr = it.mt * kTcRows + (et & 127);
                             const bool bad = (__ldcg(a.expect + t) & (int)kBad) != 0;
                             float sum = 0.0f;
 #pragma unroll
                             for (int k = 0; k < kTop; k++) {
                                 const int id = __ldcg(a.ids + t * kTop + k);
-                                sum += id >= 0 ? __ldcg(a.slots + ((size_t)t * kTop + k) * H + row) : 0.0f;
+                                sum += id >= 0 ? __ldcg(a.slots + ((size_t)t * kTop + k) * H + rr) : 0.0f;
                             }
-                            if (a.sg) sum = __fmaf_rn(__ldcg(a.shout + (size_t)t * H + row), sigmoidf_ref(__ldcg(a.sgate + t)), sum);
-                            a.out[(size_t)t * H + row] = bad ? __int_as_float(0x7fc00000) : sum;
+                            if (a.sg) sum = __fmaf_rn(__ldcg(a.shout + (size_t)t * H + rr), sigmoidf_ref(__ldcg(a.sgate + t)), sum);
+                            a.out[(size_t)t * H + rr] = bad ? __int_as_float(0x7fc00000) : sum;
                         }
                     }
                 }
