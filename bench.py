@@ -304,7 +304,7 @@ def main() -> None:
     L.call("moe_profile", 1)
     for _ in range(args.steps):
         stack.step()
-    phases = ("router", "route", "plan", "gate_up", "down", "combine")
+    phases = ("router", "route", "plan", "gate_up", "down", "combine", "experts", "decode_router")
     prof = {}
     import ctypes as C
     for i, name in enumerate(phases):
@@ -313,13 +313,17 @@ def main() -> None:
         prof[name] = (tot.value, n.value)
     L.call("moe_profile", 0)
     peaks = measured_peaks()
-    pairs = T * K
-    gate_up_bytes = sum((u + 1) * 2 * 589_824 + T * H * 4 + (pairs + T) * F * 4 for u in used) / len(used)
-    down_bytes = sum((u + 1) * 589_824 + (pairs + T) * F * 4 + (pairs + T) * H * 4 for u in used) / len(used)
-    dom = max(("gate_up", "down"), key=lambda k: prof[k][0])
-    dom_bytes = gate_up_bytes if dom == "gate_up" else down_bytes
-    dom_ms = prof[dom][0] / max(1, prof[dom][1])
+    # algorithmic bytes per launch: every used expert's gate/up/down rows (+ the
+    # shared expert) read once, x read, out written; router: its matrix and x
+    u_mean = float(np.mean(used))
+    alg_bytes = {"experts": (u_mean + 1) * EXPERT_BYTES + 2 * T * H * 4,
+                 "decode_router": (E + 1) * H * 4 + T * H * 4 + T * K * 8}
+    timed = {k: v for k, v in prof.items() if v[1] > 0 and k in alg_bytes}
+    dom = max(timed, key=lambda k: timed[k][0])
+    dom_bytes = alg_bytes[dom]
+    dom_ms = prof[dom][0] / prof[dom][1]
     achieved = dom_bytes / (dom_ms / 1e3) / 1e9
+    launches_per_step = sum(v[1] for v in prof.values()) / args.steps
     total_prof_ms = sum(v[0] for v in prof.values())
     stack_bytes = sum(layer_bytes(u, T) for u in used)
 
@@ -385,7 +389,7 @@ def main() -> None:
                    "hbm_gbs": pbytes / (pms / 1e3) / 1e9, "hbm_frac": pbytes / (pms / 1e3) / 1e9 / peaks["hbm_gbs"],
                    "tflops": flops / (pms / 1e3) / 1e12,
                    "tensor_frac": flops / (pms / 1e3) / 1e12 / peaks["bf16_tflops"],
-                   "path": "SIMT grouped dequant-GEMV (no tensor cores)"}
+                   "path": "tcgen05 tensor-core expert kernel (Q4_K codes and fp16 hi/lo activations)"}
 
     cpu = None
     if not args.no_cpu and rank == 0:
@@ -413,10 +417,11 @@ def main() -> None:
         "roofline": {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                      "frac": achieved / peaks["hbm_gbs"], "peak_source": peaks["source"] + " (MEASURED_PEAKS.json hbm_gbs)",
                      "traffic": None, "algorithmic_bytes_per_launch": dom_bytes, "avg_launch_ms": dom_ms,
-                     "phase_share": {k: v[0] / total_prof_ms for k, v in prof.items()}},
+                     "phase_share": {k: v[0] / total_prof_ms for k, v in prof.items() if v[1]},
+                     "phase_ms_per_launch": {k: v[0] / v[1] for k, v in prof.items() if v[1]}},
         "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": args.layers * nbytes,
                 "d2h_bytes_per_step": args.layers * nbytes},
-        "gpu_launches": args.steps * args.layers * 7,
+        "gpu_launches": int(round(args.steps * launches_per_step)),
         "clocks": clk.summary(),
     }
     if prefill:

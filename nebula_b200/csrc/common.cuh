@@ -87,12 +87,35 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
         : "memory");
     return ok != 0;
 }
-// Bounded wait on an mbarrier phase. try_wait suspends for a hardware time
-// slice per attempt; the attempt limit turns a lost completion into an error
-// flag instead of a hang. Returns false on timeout.
+__device__ __forceinline__ uint64_t global_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+// try_wait with a suspend-time hint: the thread sleeps until the phase
+// completes or about hint_ns elapse, so waiting warps take no issue slots.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t *bar, uint32_t parity, uint32_t hint_ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+        : "memory");
+    return ok != 0;
+}
+// Every wait on another role or another CTA gives up after this long.
+constexpr uint64_t kWaitLimitNs = 2000000000ull;
+constexpr uint32_t kWaitHintNs = 20000;
+// Bounded wait on an mbarrier phase: a lost completion becomes an error flag
+// instead of a hang. Returns false on timeout.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity, int *err_flag) {
-    for (int i = 0; i < (1 << 22); i++)
-        if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = global_ns();
+    do {
+        if (mbar_try_wait_sleep(bar, parity, kWaitHintNs)) return true;
+    } while (global_ns() - t0 < kWaitLimitNs);
     if (err_flag) atomicOr(err_flag, 1);
     return false;
 }

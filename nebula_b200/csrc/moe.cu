@@ -43,7 +43,9 @@ namespace {
 // ---------------------------------------------------------------- profiling
 // Optional CUDA-event timing of each phase of the MoE layer (qg_moe_profile).
 // Only eager launches on the legacy stream are timed; graph captures are not.
-enum Phase { kRouter, kRoute, kPlan, kGateUp, kDown, kCombine, kPhases };
+// kExpertsFused: one kernel doing gate/up, SwiGLU, down and the combine;
+// kDecodeRouter: one kernel doing the router GEMV, top-10 and the plan.
+enum Phase { kRouter, kRoute, kPlan, kGateUp, kDown, kCombine, kExpertsFused, kDecodeRouter, kPhases };
 struct Profiler {
     bool on = false;
     std::vector<cudaEvent_t> pool;
@@ -59,6 +61,19 @@ struct Profiler {
     }
 };
 Profiler g_prof;
+
+// Decode path: the router/plan kernel and the expert kernel timed separately.
+int dec_run_timed(const DecArgs &a, cudaStream_t st) {
+    cudaEvent_t e0, e1, e2;
+    if (!g_prof.on || st != 0 || !(e0 = g_prof.take()) || !(e1 = g_prof.take()) || !(e2 = g_prof.take()))
+        return dec_run(a, st);
+    cudaEventRecord(e0, st);
+    int rc = dec_run(a, st, e1);
+    cudaEventRecord(e2, st);
+    g_prof.spans.push_back({kDecodeRouter, {e0, e1}});
+    g_prof.spans.push_back({kExpertsFused, {e1, e2}});
+    return rc;
+}
 
 struct Span {
     int phase;
@@ -117,7 +132,7 @@ Layout layout(int T, int H, int F) {
     L.sub = take(sizeof(SubJob) * (size_t)max_subjobs(T));
     L.nsub = take(sizeof(int));
     L.mid16 = take(sizeof(__half) * ((size_t)T * kTop + T) * 2 * F);
-    L.midinv = take(sizeof(float) * ((size_t)T * kTop + T));
+    L.midinv = take(sizeof(float) * ((size_t)T * kTop + T) * (F / 128));
     L.msum = take(sizeof(float) * ((size_t)T * kTop + T) * (F / 32));
     L.gudone = take(sizeof(int) * (size_t)max_subjobs(T));
     L.tilecnt = take(sizeof(int) * (size_t)T * (H / kTcRows));
@@ -889,7 +904,7 @@ int run_experts(float *out, const float *x, const int *ids, const float *wts, in
         t.pairs = pl.pairs, t.wts = wts, t.ids = ids;
         t.expect = reinterpret_cast<int *>(base + L.expect);
         t.sgate = has_shared ? sgate : nullptr;
-        t.mid = mid, t.mid16 = reinterpret_cast<__half *>(base + L.mid16);
+        t.mid16 = reinterpret_cast<__half *>(base + L.mid16);
         t.midinv = reinterpret_cast<float *>(base + L.midinv);
         t.msum = reinterpret_cast<float *>(base + L.msum);
         t.slots = slots, t.shout = shared, t.out = out;
@@ -910,7 +925,7 @@ int run_experts(float *out, const float *x, const int *ids, const float *wts, in
                                         const_cast<float *>(t.xsum), st))
                 return rc;
         }
-        Span sp(kGateUp, st);
+        Span sp(kExpertsFused, st);
         return tc_launch(t, maps, st, false);
     }
 
@@ -1003,8 +1018,7 @@ extern "C" int qg_moe_routed(float *out, const float *x, const int *ids, const f
         a.gate = static_cast<const unsigned char *>(gate);
         a.up = static_cast<const unsigned char *>(up);
         a.down = static_cast<const unsigned char *>(down);
-        Span sp(kGateUp, launch_stream);
-        return dec_run(a, launch_stream);
+        return dec_run_timed(a, launch_stream);
     }
     return run_experts(out, x, ids, weights, tokens, gate, gt, up, ut, down, dt, nullptr, 0, nullptr, 0, nullptr, 0,
                        nullptr, 0, hidden, ffn, workspace, launch_stream);
@@ -1035,8 +1049,7 @@ extern "C" int qg_moe_layer(float *out, int *ids_out, float *weights_out, const 
         a.sg = static_cast<const unsigned char *>(sg);
         a.su = static_cast<const unsigned char *>(su);
         a.sd = static_cast<const unsigned char *>(sd);
-        Span sp(kGateUp, st);
-        return dec_run(a, st);
+        return dec_run_timed(a, st);
     }
     Layout L = layout(tokens, hidden, ffn);
     char *base = static_cast<char *>(workspace);

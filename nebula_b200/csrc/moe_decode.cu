@@ -77,10 +77,11 @@ __device__ __forceinline__ int pair_pos(int l) {
 }
 
 __device__ bool wait_geq(const int *p, int target, int *err) {
-    for (int i = 0; i < (1 << 22); i++) {
+    const uint64_t t0 = global_ns();
+    do {
         if (ld_acquire(p) >= target) return true;
         __nanosleep(64);
-    }
+    } while (global_ns() - t0 < kWaitLimitNs);
     atomicOr(err, 2);
     return false;
 }
@@ -750,12 +751,12 @@ int launch_k1(const DecArgs &a, cudaStream_t st, size_t smem) {
 }
 
 template <int QG, int QD>
-int launch_k2(const DecArgs &a, cudaStream_t st, int ctas) {
+int launch_k2(const DecArgs &a, cudaStream_t st, int ctas, bool pdl) {
     auto k = dec_experts_kernel<QG, QD>;
     const size_t smem = (size_t)kStages * a.stage_bytes;
     int rc = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (rc) return rc;
-    return launch_pdl(k, dim3(ctas), dim3(kK2Threads), smem, st, true, a);
+    return launch_pdl(k, dim3(ctas), dim3(kK2Threads), smem, st, pdl, a);
 }
 
 int sm_count() {
@@ -799,7 +800,7 @@ DecLayout dec_layout(int T, int H, int F) {
     L.sub = take(sizeof(SubJob) * (kExperts + 1));
     L.nsub = take(sizeof(int));
     L.mid16 = take(sizeof(__half) * (T * kTop + T) * 2 * F);
-    L.midinv = take(sizeof(float) * (T * kTop + T));
+    L.midinv = take(sizeof(float) * (T * kTop + T) * (F / 128));
     L.total = p;
     return L;
 }
@@ -820,7 +821,7 @@ bool dec_supported(int T, int H, int F, int QG, int QD) {
     return true;
 }
 
-int dec_run(const DecArgs &in, cudaStream_t st) {
+int dec_run(const DecArgs &in, cudaStream_t st, cudaEvent_t split) {
     DecArgs a = in;
     a.use_tc = tc_supported(a.H, a.F, a.QG, a.QD) && a.H / kTcRows <= 64;
     const size_t grb = a.grb, drb = a.drb;
@@ -844,6 +845,9 @@ int dec_run(const DecArgs &in, cudaStream_t st) {
     }
 #undef NB_K1
     if (rc) return rc;
+    // profiling: an event between the two kernels, which then run without overlap
+    const bool pdl = split == nullptr;
+    if (split && (rc = cudaEventRecord(split, st))) return rc;
     if (a.use_tc) {
         TcArgs t{};
         t.T = a.T, t.H = a.H, t.F = a.F;
@@ -852,19 +856,19 @@ int dec_run(const DecArgs &in, cudaStream_t st) {
         t.x16 = a.x16, t.xinv = a.xinv, t.xsum = a.xsum;
         t.sub = a.sub, t.n_sub = a.n_sub, t.shared_subs = a.sg ? 1 : 0;
         t.pairs = a.pairs, t.wts = a.wts, t.ids = a.ids, t.expect = a.expect, t.sgate = a.sg ? a.sgate : nullptr;
-        t.mid = a.mid, t.mid16 = a.mid16, t.midinv = a.midinv, t.msum = a.msum;
+        t.mid16 = a.mid16, t.midinv = a.midinv, t.msum = a.msum;
         t.slots = a.slots, t.shout = a.shout, t.out = a.out;
         t.queue = &a.ctr->tc_queue, t.tc_ticket = &a.ctr->tc_ticket;
         t.gu_done = a.ctr->gu_done, t.tilecnt = a.ctr->tilecnt, t.err = &a.hdr->error;
         TcMaps maps;
         if ((rc = tc_make_maps(t, maps))) return rc;
-        return tc_launch(t, maps, st, true);
+        return tc_launch(t, maps, st, pdl);
     }
     const int ctas = sm_count();
-    if (a.QG == 12 && a.QD == 12) return launch_k2<12, 12>(a, st, ctas);
-    if (a.QG == 12 && a.QD == 20) return launch_k2<12, 20>(a, st, ctas);
-    if (a.QG == 20 && a.QD == 12) return launch_k2<20, 12>(a, st, ctas);
-    return launch_k2<20, 20>(a, st, ctas);
+    if (a.QG == 12 && a.QD == 12) return launch_k2<12, 12>(a, st, ctas, pdl);
+    if (a.QG == 12 && a.QD == 20) return launch_k2<12, 20>(a, st, ctas, pdl);
+    if (a.QG == 20 && a.QD == 12) return launch_k2<20, 12>(a, st, ctas, pdl);
+    return launch_k2<20, 20>(a, st, ctas, pdl);
 }
 
 }  // namespace nb

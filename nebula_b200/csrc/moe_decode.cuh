@@ -51,6 +51,8 @@ struct DecArgs {
 };
 
 bool dec_supported(int T, int H, int F, int QG, int QD);
-int dec_run(const DecArgs &a, cudaStream_t st);
+// split != null (profiling): recorded between the router/plan kernel and the
+// expert kernel, which is then launched without programmatic overlap.
+int dec_run(const DecArgs &a, cudaStream_t st, cudaEvent_t split = nullptr);
 
 }  // namespace nb

@@ -3,30 +3,44 @@
 //
 // Work items (claimed from a device queue, shared expert first): a gate/up
 // tile = 128 rows of W_gate and of W_up of one expert x one token tile of up
-// to 64 tokens; a down tile = 128 rows of W_down x the same token tile.
+// to 48 tokens; a down tile = 128 rows of W_down x the same token tile.
 //
 // The contraction runs on the 5th-generation tensor cores:
 //   A = sc_g * q_k    fp16, exact (integers <= 945), decoded from the raw Q4_K
-//                     bytes by four converter warps into the UMMA K-major
-//                     no-swizzle layout (8x8 core matrices);
-//   B = [x_hi | x_lo] fp16, x*s = x_hi + x_lo/2048 with a per-token power of
-//                     two s (22-bit precision), copied from a prepared buffer;
+//                     bytes by four converter warps straight into tensor
+//                     memory (tcgen05.st; lane = weight row), so A never
+//                     crosses shared memory;
+//   B = [v_hi | v_lo] fp16 in shared memory (UMMA K-major, no swizzle),
+//                     v*s = v_hi + v_lo/2048 with a power of two s (22-bit
+//                     precision): the token's activations (one s per token)
+//                     for gate/up, the SwiGLU output (one s per token and
+//                     128-value tile) for down;
 //   D = A B^T         fp32 in tensor memory, accumulated per 256-value Q4_K
-//                     superblock into one of two TMEM buffers.
+//                     superblock (down: per 128-value half, one per scale)
+//                     into one of two TMEM buffers.
+// A tcgen05.mma with N <= 64 costs about the same issue time whatever N is, so
+// two threads issue them: one for W_gate (or the first half of a down
+// superblock), one for W_up (or the second half).
 // Eight epilogue warps read each superblock's D back (tcgen05.ld), apply the
-// superblock scale d and the dmin*m_g*sum(x) term in fp32 and accumulate in
-// registers; gate/up tiles finish with SiLU(g)*u, down tiles with the route
-// weight, and the last contribution to a (token, 128-row tile) sums the ten
-// slots in router-rank order plus the gated shared expert
+// superblock scale d and the dmin*m_g*sum(v) term in fp32 and accumulate in
+// registers. A gate/up tile ends with SiLU(g)*u, whose fp16 hi/lo split, scale
+// and 32-value group sums it writes directly for the down tiles; a down tile
+// ends with the route weight, and the last contribution to a (token, 128-row
+// tile) sums the ten slots in router-rank order plus the gated shared expert
 // (qwen/cpu.c:209-231, qwen/gpu.cu:552).
 //
 // Raw weight bytes stream with 2-D TMA tensor copies (a 144-byte x 128-row
-// box = one superblock of 128 rows) into a two-stage ring. Warp roles:
+// box = one superblock of 128 rows) into a three-stage ring; B rows stream
+// with cp.async into a three-stage ring run ahead by their own warp. Roles:
 //   warp 0 lane 0   producer: claims items, issues TMA
-//   warp 1          TMEM owner; lane 0 issues tcgen05.mma and commits
-//   warps 2-5       converters (thread = weight row): A tiles, B copies
-//   warps 6-13      epilogue (warp w reads TMEM lanes 32*(w%4).., half the
-//                   tokens each)
+//   warp 1          TMEM owner; lane 0 issues the gate (first-half) MMAs
+//   warp 2          B stager: token table, B rows, per-superblock group sums
+//   warp 3 lane 0   issues the up (second-half) MMAs
+//   warps 4-11      converters (thread = weight row; warps 4-7 the low
+//                   nibbles and the row scales, warps 8-11 the high nibbles)
+//   warps 12-19     epilogue (warp w reads TMEM lanes 32*(w%4).., half the
+//                   tokens each); a tile's per-token outputs go through a
+//                   shared buffer so the per-token loops stay short
 // Every wait is bounded; on a timeout the CTA raises the error word, stops
 // taking work, drains its copies and MMAs, frees TMEM and exits.
 #include <algorithm>
@@ -37,16 +51,32 @@ using namespace nb;
 
 namespace {
 
-constexpr int kWarps = 14, kThreads = kWarps * 32;
-constexpr int kConvWarp0 = 2, kEpiWarp0 = 6;
-constexpr int kSbBytes = kTcRows * 144;          // one superblock of 128 Q4_K rows
-constexpr int kRawStage = 2 * kSbBytes;          // gate + up
-constexpr int kABytes = kTcRows * 64 * 2;        // 128 rows x 64 halves
-constexpr int kBBytes = 2 * kTcTok * 64 * 2;     // up to 128 B rows x 64 halves
-constexpr int kScRows = 2 * kTcRows * 16;        // d, dmin, m[8] per row per matrix
-constexpr int kScSlot = kScRows + 8 * kTcTok * 4; // + the superblock's 8 group sums per token
-constexpr int kOffRaw = 0, kOffA = kOffRaw + 2 * kRawStage, kOffB = kOffA + 2 * 2 * kABytes,
-              kOffSc = kOffB + 2 * kBBytes, kSmem = kOffSc + 4 * kScSlot;
+constexpr int kWarps = 20, kThreads = kWarps * 32;
+constexpr int kProdWarp = 0, kMmaWarp = 1, kStageWarp = 2, kMma2Warp = 3, kConvWarp0 = 4, kEpiWarp0 = 12;
+constexpr int kConvWarps = 8, kEpiWarps = 8;
+// Registers: launched at 96 per thread (20 warps x 32 x 96 = 61440); warpgroups
+// 0-2 (producer, issuers, stager, converters) give theirs down to 64 and the
+// two epilogue warpgroups take them up to 144: 12*32*64 + 8*32*144 = 61440.
+constexpr int kRegsLaunch = 96, kRegsLow = 64, kRegsEpi = 144;
+static_assert((kWarps - kEpiWarps) * kRegsLow + kEpiWarps * kRegsEpi == kWarps * kRegsLaunch, "register split");
+static_assert(kEpiWarp0 % 4 == 0 && kEpiWarps % 4 == 0, "register split is per warpgroup");
+constexpr int kSbBytes = kTcRows * 144;           // one superblock of 128 Q4_K rows
+constexpr int kRawStage = 2 * kSbBytes;           // gate + up
+constexpr int kRawStages = 3;
+constexpr int kBBytes = 2 * kTcTok * 64 * 2;      // up to 96 B rows x 64 halves
+constexpr int kBStages = 4;
+constexpr int kScRows = 2 * kTcRows * 16;         // d, dmin, m[8] per row per matrix
+constexpr int kScXs = 8 * kTcTok * 4;             // the superblock's 8 group sums per token [token][8]
+constexpr int kScSlot = kScRows + kScXs + 2 * kTcTok * 4;  // + 1/s per token per 128-value half
+constexpr int kVBytes = kTcTok * kTcRows * 4;     // one tile's per-token outputs [token][row]
+constexpr int kOffRaw = 0, kOffB = kOffRaw + kRawStages * kRawStage, kOffSc = kOffB + kBStages * kBBytes,
+              kOffV = kOffSc + 4 * kScSlot, kSmem = kOffV + kVBytes;
+// Tensor memory (512 columns): D[db][m] at (db*2+m)*kDCols, A[ab][m] (32
+// columns = 64 fp16 of one 64-value chunk) at kACol0 + (ab*2+m)*32.
+constexpr int kDCols = 2 * kTcTok;
+constexpr int kACol0 = 4 * kDCols;
+static_assert(kACol0 + 4 * 32 <= 512, "tensor memory budget");
+static_assert(kSmem % 16 == 0 && kScSlot % 16 == 0, "alignment");
 constexpr uint32_t kBad = 1u << 16;
 
 enum { kEnd = 0, kGU = 1, kDN = 2 };
@@ -55,12 +85,13 @@ struct Item {
 };
 
 struct Bars {
-    uint64_t item_full[4], item_empty[4];
-    uint64_t raw_full[2], raw_empty[2];
-    uint64_t ab_full[2], ab_empty[2];
+    uint64_t item_full[4], item_empty[4], tab_full[4];
+    uint64_t raw_full[kRawStages], raw_empty[kRawStages];
+    uint64_t a_full[2], a_empty[2];
+    uint64_t b_full[kBStages], b_empty[kBStages];
     uint64_t d_full[2], d_empty[2];
     uint64_t sc_full[4], sc_empty[4];
-    uint64_t mma_done;
+    uint64_t mma_done[2];
 };
 
 __device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
@@ -74,15 +105,19 @@ __device__ __forceinline__ int ld_acquire(const int *p) {
     return v;
 }
 __device__ __forceinline__ void bar_named(int id, int n) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory"); }
+__device__ __forceinline__ void regs_dec() { asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsLow)); }
+__device__ __forceinline__ void regs_inc() { asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegsEpi)); }
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
 // Bounded wait used by every role; `abort` is the CTA-wide stop flag.
 __device__ __forceinline__ bool wait_phase(uint64_t *bar, uint32_t parity, volatile int *abort, int *err) {
-    for (int i = 0; i < (1 << 21); i++) {
-        if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = global_ns();
+    do {
+        if (mbar_try_wait_sleep(bar, parity, kWaitHintNs)) return true;
         if (*abort) return false;
-    }
+    } while (global_ns() - t0 < kWaitLimitNs);
     *abort = 1;
     atomicOr(err, 4);
     return false;
@@ -90,16 +125,21 @@ __device__ __forceinline__ bool wait_phase(uint64_t *bar, uint32_t parity, volat
 
 // Bounded wait that ignores the stop flag: used to drain work already in flight.
 __device__ __forceinline__ bool wait_drain(uint64_t *bar, uint32_t parity) {
-    for (int i = 0; i < (1 << 21); i++)
-        if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = global_ns();
+    do {
+        if (mbar_try_wait_sleep(bar, parity, kWaitHintNs)) return true;
+    } while (global_ns() - t0 < kWaitLimitNs);
     return false;
 }
 
+// Bounded wait on a counter written by other CTAs.
 __device__ bool wait_geq_int(const int *p, int target, int *err) {
-    for (int i = 0; i < (1 << 22); i++) {
+    const uint64_t t0 = global_ns();
+    do {
         if (ld_acquire(p) >= target) return true;
         __nanosleep(64);
-    }
+    } while (global_ns() - t0 < kWaitLimitNs);
     atomicOr(err, 4);
     return false;
 }
@@ -114,7 +154,8 @@ __device__ __forceinline__ void tma_2d(void *dst, const CUtensorMap *map, int x,
 
 // UMMA shared-memory descriptor, K-major, no swizzle: 8x8 core matrices of
 // 128 contiguous bytes; LBO = distance between the two K-halves of one MMA,
-// SBO = distance between 8-row groups.
+// SBO = distance between 8-row groups. Adding n to the descriptor advances
+// its start address by 16*n bytes.
 __device__ __forceinline__ uint64_t umma_desc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
     return (uint64_t)((addr >> 4) & 0x3FFF) | ((uint64_t)((lbo >> 4) & 0x3FFF) << 16) |
            ((uint64_t)((sbo >> 4) & 0x3FFF) << 32) | ((uint64_t)1 << 46);
@@ -123,68 +164,91 @@ __device__ __forceinline__ uint64_t umma_desc(uint32_t addr, uint32_t lbo, uint3
 __device__ __forceinline__ uint32_t idesc_f16(int M, int N) {
     return (1u << 4) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
-__device__ __forceinline__ void mma_f16(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+// D (tmem) [+]= A (tmem) * B (smem descriptor)^T
+__device__ __forceinline__ void mma_ts(uint32_t d, uint32_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
     asm volatile(
         "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d),
-        "l"(a), "l"(b), "r"(idesc), "r"(acc)
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d),
+        "r"(a), "l"(b), "r"(idesc), "r"(acc)
         : "memory");
+}
+__device__ __forceinline__ void mma_ts1(uint32_t d, uint32_t a, uint64_t b, uint32_t idesc) {
+    asm volatile("tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, 1;" ::"r"(d), "r"(a), "l"(b), "r"(idesc)
+                 : "memory");
 }
 __device__ __forceinline__ void mma_commit(uint64_t *bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
                  : "memory");
 }
-__device__ __forceinline__ void tmem_ld8(uint32_t addr, float (&v)[8]) {
-    uint32_t r[8];
+__device__ __forceinline__ void tmem_ld8_nw(uint32_t addr, uint32_t (&r)[8]) {
     asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
                  : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
                  : "r"(addr));
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-    for (int j = 0; j < 8; j++) v[j] = __uint_as_float(r[j]);
 }
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+// 32 consecutive columns of this thread's lane
+__device__ __forceinline__ void tmem_st32(uint32_t addr, const uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+        "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(addr),
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+        "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]),
+        "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]),
+        "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+        : "memory");
+}
+__device__ __forceinline__ void tmem_st16(uint32_t addr, const uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(addr),
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+        "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+        : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void cp_async16(void *dst, const void *src) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
 }
+__device__ __forceinline__ void cp_async4(void *dst, const void *src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
+// Named barrier over n threads that also ANDs a predicate across them.
+__device__ __forceinline__ bool bar_all(int id, int n, bool ok) {
+    int r;
+    asm volatile("{\n\t.reg .pred p, q;\n\tsetp.ne.b32 p, %1, 0;\n\tbar.red.and.pred q, %2, %3, p;\n\tselp.b32 %0, 1, 0, q;\n\t}"
+                 : "=r"(r) : "r"((int)ok), "r"(id), "r"(n) : "memory");
+    return r != 0;
+}
 
-// Q4_K: decode unit c (values 64c..64c+63 of a superblock) of one 144-byte
-// row into four 16-byte A rows (k-slots 8kb..8kb+7 for kb = 0..7, value
-// 64c + k). Low nibbles of bytes 0..31 are values 0..31 (scale sc[2c]), high
-// nibbles are values 32..63 (scale sc[2c+1]); each half is sc*q exactly.
-__device__ __forceinline__ void q4k_unit_to_a(const unsigned char *row, int c, unsigned char *a_row, int a_kstride) {
+// Q4_K: decode half `nib` of unit c of one 144-byte row into 16 tensor-memory
+// columns. Unit c holds values 64c..64c+63: the low nibbles of its 32 bytes
+// are values 64c+l (scale sc[2c]), the high nibbles 64c+32+l (scale sc[2c+1]).
+// Column i of the unit holds values 64c+2i (low half) and 64c+2i+1, so half 0
+// fills columns 0..15 and half 1 columns 16..31. Each value is sc*q exactly:
+// (1024 + q) or (1024 + 16 q) come out of the nibbles as fp16 bit patterns
+// and one half-precision FMA per pair removes the offset and applies sc.
+__device__ __forceinline__ void q4k_half_cols(const unsigned char *row, int c, int nib, uint32_t (&r)[16]) {
     const uint4 hd = *reinterpret_cast<const uint4 *>(row);
     const unsigned char *sc = reinterpret_cast<const unsigned char *>(&hd) + 4;
-    int s0, m0, s1, m1;
-    k_scale_min(sc, 2 * c, s0, m0);
-    k_scale_min(sc, 2 * c + 1, s1, m1);
-    (void)m0;
-    (void)m1;
-    const __half2 sc_lo = __half2half2(__int2half_rn(s0)), neg_lo = __half2half2(__int2half_rn(-1024 * s0));
-    const __half2 sc_hi = __half2half2(__float2half_rn((float)s1 * 0.0625f)), neg_hi = __half2half2(__int2half_rn(-64 * s1));
+    int s, m;
+    k_scale_min(sc, 2 * c + nib, s, m);
+    (void)m;
+    const __half2 mul = __half2half2(nib ? __float2half_rn((float)s * 0.0625f) : __int2half_rn(s));
+    const __half2 off = __half2half2(__int2half_rn(nib ? -64 * s : -1024 * s));
+    const uint32_t mask = nib ? 0x00F000F0u : 0x000F000Fu;
     const uint4 q0 = *reinterpret_cast<const uint4 *>(row + 16 + 32 * c);
     const uint4 q1 = *reinterpret_cast<const uint4 *>(row + 32 + 32 * c);
     const uint32_t w[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
 #pragma unroll
-    for (int kb = 0; kb < 4; kb++) {
-        uint32_t lo[4], hi[4];
-#pragma unroll
-        for (int h = 0; h < 2; h++) {
-            const uint32_t word = w[2 * kb + h];
-            const uint32_t t01 = __byte_perm(word, 0, 0x4140), t23 = __byte_perm(word, 0, 0x4342);
-            const uint32_t ts[2] = {t01, t23};
-#pragma unroll
-            for (int p = 0; p < 2; p++) {
-                uint32_t vl = (ts[p] & 0x000F000Fu) | 0x64006400u;  // 1024 + q
-                uint32_t vh = (ts[p] & 0x00F000F0u) | 0x64006400u;  // 1024 + 16 q
-                __half2 rl = __hfma2(*reinterpret_cast<__half2 *>(&vl), sc_lo, neg_lo);
-                __half2 rh = __hfma2(*reinterpret_cast<__half2 *>(&vh), sc_hi, neg_hi);
-                lo[2 * h + p] = *reinterpret_cast<uint32_t *>(&rl);
-                hi[2 * h + p] = *reinterpret_cast<uint32_t *>(&rh);
-            }
-        }
-        *reinterpret_cast<uint4 *>(a_row + kb * a_kstride) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
-        *reinterpret_cast<uint4 *>(a_row + (kb + 4) * a_kstride) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+    for (int i = 0; i < 8; i++) {
+        const uint32_t t01 = __byte_perm(w[i], 0, 0x4140), t23 = __byte_perm(w[i], 0, 0x4342);
+        uint32_t v0 = (t01 & mask) | 0x64006400u, v1 = (t23 & mask) | 0x64006400u;
+        __half2 h0 = __hfma2(*reinterpret_cast<__half2 *>(&v0), mul, off);
+        __half2 h1 = __hfma2(*reinterpret_cast<__half2 *>(&v1), mul, off);
+        r[2 * i] = *reinterpret_cast<uint32_t *>(&h0);
+        r[2 * i + 1] = *reinterpret_cast<uint32_t *>(&h1);
     }
 }
 
@@ -203,31 +267,38 @@ __device__ __forceinline__ uint4 q4k_row_scales(const unsigned char *row) {
     return make_uint4(__float_as_uint(d), __float_as_uint(dmin), m4[0], m4[1]);
 }
 
-// Per-item token table, filled once per item (shared by all roles).
+// sum_g m_g * xs[token][g] for tokens j and j+1 (xs: 8 group sums per token)
+__device__ __forceinline__ float2 mterm2(const float (&mg)[8], const float *xs, int j) {
+    const float4 a0 = *reinterpret_cast<const float4 *>(xs + j * 8), a1 = *reinterpret_cast<const float4 *>(xs + j * 8 + 4);
+    const float4 b0 = *reinterpret_cast<const float4 *>(xs + j * 8 + 8), b1 = *reinterpret_cast<const float4 *>(xs + j * 8 + 12);
+    float2 t = __fmul2_rn(make_float2(mg[0], mg[0]), make_float2(a0.x, b0.x));
+    t = __ffma2_rn(make_float2(mg[1], mg[1]), make_float2(a0.y, b0.y), t);
+    t = __ffma2_rn(make_float2(mg[2], mg[2]), make_float2(a0.z, b0.z), t);
+    t = __ffma2_rn(make_float2(mg[3], mg[3]), make_float2(a0.w, b0.w), t);
+    t = __ffma2_rn(make_float2(mg[4], mg[4]), make_float2(a1.x, b1.x), t);
+    t = __ffma2_rn(make_float2(mg[5], mg[5]), make_float2(a1.y, b1.y), t);
+    t = __ffma2_rn(make_float2(mg[6], mg[6]), make_float2(a1.z, b1.z), t);
+    t = __ffma2_rn(make_float2(mg[7], mg[7]), make_float2(a1.w, b1.w), t);
+    return t;
+}
+
+// Per-item token table, filled by the B stager once per item.
 struct __align__(16) TokTab {
     int tok[kTcTok];   // token index
     int src[kTcTok];   // B source row, in halves: x16 row (gate/up) or mid16 row (down)
-    int mrow[kTcTok];  // mid row written (gate/up) or read (down)
+    int mrow[kTcTok];  // SwiGLU-output row written (gate/up) or read (down)
     int slot[kTcTok];  // routed slot t*10+k (down)
     float w[kTcTok];   // route weight (down)
-    float inv[kTcTok]; // 1/s of the B row (filled by the converters)
 };
-
-__device__ __forceinline__ void tmem_ld8_nw(uint32_t addr, uint32_t (&r)[8]) {
-    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
-                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
-                 : "r"(addr));
-}
-__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
 __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a, const __grid_constant__ TcMaps maps) {
     extern __shared__ __align__(1024) unsigned char smem[];
     __shared__ Bars bars;
     __shared__ Item items[4];
     __shared__ TokTab tabs[4];
+    __shared__ float s_scale[kTcTok];  // power-of-two scale per token of one gate/up tile
     __shared__ uint32_t tmem_base;
     __shared__ volatile int abort_flag;
-    __shared__ int s_flag;
     __shared__ int s_combine[kTcTok];
     __shared__ int s_ncombine;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -237,23 +308,30 @@ __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a,
     if (tid == 0) {
         for (int i = 0; i < 4; i++) {
             mbar_init(&bars.item_full[i], 1);
-            mbar_init(&bars.item_empty[i], 4 + 1 + 8);
-            mbar_init(&bars.sc_full[i], 4);
-            mbar_init(&bars.sc_empty[i], 8);
+            mbar_init(&bars.item_empty[i], 2 + 1 + kConvWarps + kEpiWarps);  // issuers, stager, converters, epilogue
+            mbar_init(&bars.tab_full[i], 1);
+            mbar_init(&bars.sc_full[i], 4 + 1);  // low-nibble converters (row scales), stager (group sums, 1/s)
+            mbar_init(&bars.sc_empty[i], kEpiWarps);
         }
-        mbar_init(&bars.mma_done, 1);
-        for (int i = 0; i < 2; i++) {
+        for (int i = 0; i < kRawStages; i++) {
             mbar_init(&bars.raw_full[i], 1);
-            mbar_init(&bars.raw_empty[i], 4);
-            mbar_init(&bars.ab_full[i], 4);
-            mbar_init(&bars.ab_empty[i], 1);
-            mbar_init(&bars.d_full[i], 1);
-            mbar_init(&bars.d_empty[i], 8);
+            mbar_init(&bars.raw_empty[i], kConvWarps);
+        }
+        for (int i = 0; i < 2; i++) {
+            mbar_init(&bars.a_full[i], kConvWarps);
+            mbar_init(&bars.a_empty[i], 2);
+            mbar_init(&bars.d_full[i], 2);
+            mbar_init(&bars.d_empty[i], kEpiWarps);
+            mbar_init(&bars.mma_done[i], 1);
+        }
+        for (int i = 0; i < kBStages; i++) {
+            mbar_init(&bars.b_full[i], 1);
+            mbar_init(&bars.b_empty[i], 2);
         }
         abort_flag = 0;
         fence_mbar_init();
     }
-    if (warp == 1) {
+    if (warp == kMmaWarp) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(smem_u32(&tmem_base)));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
     }
@@ -264,114 +342,107 @@ __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a,
     const uint32_t tmem = tmem_base;
     int *err = a.err;
 
-    if (warp == 0) {
-        // ------------------------------------------------------ producer warp
-        bool planned = false;
-        int nsub = a.shared_subs;
-        int gsb = 0;
-        const int S_gu = a.shared_subs * gu_mt;
-        for (int seq = 0;; seq++) {
-            const int slot = seq & 3;
-            int idx = 1 << 30;
-            if (lane == 0) {
-                bool ok = seq < 4 || wait_phase(&bars.item_empty[slot], ((seq >> 2) - 1) & 1, &abort_flag, err);
+    if (warp == kProdWarp) {
+        // ------------------------------------------------------ producer
+        regs_dec();
+        if (lane == 0) {
+            bool planned = false;
+            int nsub = a.shared_subs, gsb = 0;
+            const int S_gu = a.shared_subs * gu_mt;
+            for (int seq = 0;; seq++) {
+                const int slot = seq & 3;
+                int idx = 1 << 30;
+                const bool ok = seq < 4 || wait_phase(&bars.item_empty[slot], ((seq >> 2) - 1) & 1, &abort_flag, err);
                 if (ok && !abort_flag) idx = atomicAdd(a.queue, 1);
                 if (idx >= S_gu && idx != (1 << 30) && !planned) {
-                    grid_dep_wait();
+                    grid_dep_wait();  // routed work: the plan comes from the preceding kernel
                     nsub = __ldcg(a.n_sub);
                     planned = true;
                 }
-            }
-            idx = __shfl_sync(0xffffffffu, idx, 0);
-            nsub = __shfl_sync(0xffffffffu, nsub, 0);
-            if (idx >= S_gu && idx != (1 << 30)) grid_dep_wait();
-            Item it{kEnd, 0, 0, -1, 0, 0, 0};
-            const int total_gu = nsub * gu_mt, total_dn = nsub * dn_mt;
-            if (idx < total_gu) {
-                it.kind = kGU, it.sub = idx / gu_mt, it.mt = idx % gu_mt;
-            } else if (idx < total_gu + total_dn) {
-                it.kind = kDN, it.sub = (idx - total_gu) / dn_mt, it.mt = (idx - total_gu) % dn_mt;
-            }
-            if (it.kind != kEnd) {
-                if (it.sub < a.shared_subs) {  // known without the routing
-                    it.expert = -1, it.tok0 = it.sub * kTcTok, it.n = min(kTcTok, T - it.tok0), it.first = 0;
-                } else {
-                    it.expert = __ldcg(&a.sub[it.sub].expert);
-                    it.first = __ldcg(&a.sub[it.sub].first);
-                    it.n = __ldcg(&a.sub[it.sub].n);
+                Item it{kEnd, 0, 0, -1, 0, 0, 0};
+                const int total_gu = nsub * gu_mt, total_dn = nsub * dn_mt;
+                if (idx < total_gu) {
+                    it.kind = kGU, it.sub = idx / gu_mt, it.mt = idx % gu_mt;
+                } else if (idx < total_gu + total_dn) {
+                    it.kind = kDN, it.sub = (idx - total_gu) / dn_mt, it.mt = (idx - total_gu) % dn_mt;
                 }
-                TokTab &tb = tabs[slot];
-                for (int j = lane; j < it.n; j += 32) {
-                    const bool sh = it.expert < 0;
-                    const int sl = sh ? 0 : __ldcg(a.pairs + it.first + j);
-                    const int tok = sh ? it.tok0 + j : sl / kTop;
-                    const int mrow = sh ? T * kTop + it.tok0 + j : it.first + j;
-                    tb.tok[j] = tok;
-                    tb.mrow[j] = mrow;
-                    tb.src[j] = it.kind == kGU ? tok * 2 * H : mrow * 2 * F;
-                    tb.slot[j] = sl;
-                    tb.w[j] = (sh || it.kind == kGU) ? 0.0f : __ldcg(a.wts + sl);
-                }
-            }
-            __syncwarp();
-            if (lane == 0) {
-                items[slot] = it;
-                arrive(&bars.item_full[slot]);
                 if (it.kind != kEnd) {
-                    const int nsb = it.kind == kGU ? gu_sb : dn_sb;
-                    for (int sb = 0; sb < nsb; sb++, gsb++) {
-                        const int st = gsb & 1;
-                        if (gsb >= 2 && !wait_phase(&bars.raw_empty[st], ((gsb >> 1) - 1) & 1, &abort_flag, err)) break;
-                        unsigned char *dst = smem + kOffRaw + st * kRawStage;
-                        if (it.kind == kGU) {
-                            const int y = (it.expert < 0 ? 0 : it.expert * F) + it.mt * kTcRows;
-                            mbar_arrive_expect_tx(&bars.raw_full[st], 2 * kSbBytes);
-                            tma_2d(dst, it.expert < 0 ? &maps.sg : &maps.gate, sb * 144, y, &bars.raw_full[st]);
-                            tma_2d(dst + kSbBytes, it.expert < 0 ? &maps.su : &maps.up, sb * 144, y, &bars.raw_full[st]);
-                        } else {
-                            const int y = (it.expert < 0 ? 0 : it.expert * H) + it.mt * kTcRows;
-                            mbar_arrive_expect_tx(&bars.raw_full[st], kSbBytes);
-                            tma_2d(dst, it.expert < 0 ? &maps.sd : &maps.down, sb * 144, y, &bars.raw_full[st]);
-                        }
+                    if (it.sub < a.shared_subs) {  // known without the routing
+                        it.expert = -1, it.tok0 = it.sub * kTcTok, it.n = min(kTcTok, T - it.tok0), it.first = 0;
+                    } else {
+                        it.expert = __ldcg(&a.sub[it.sub].expert);
+                        it.first = __ldcg(&a.sub[it.sub].first);
+                        it.n = __ldcg(&a.sub[it.sub].n);
                     }
                 }
+                items[slot] = it;
+                arrive(&bars.item_full[slot]);
+                if (it.kind == kEnd) break;
+                const int nsb = it.kind == kGU ? gu_sb : dn_sb;
+                for (int sb = 0; sb < nsb; sb++, gsb++) {
+                    const int st = gsb % kRawStages;
+                    if (gsb >= kRawStages &&
+                        !wait_phase(&bars.raw_empty[st], (gsb / kRawStages - 1) & 1, &abort_flag, err))
+                        break;
+                    unsigned char *dst = smem + kOffRaw + st * kRawStage;
+                    if (it.kind == kGU) {
+                        const int y = (it.expert < 0 ? 0 : it.expert * F) + it.mt * kTcRows;
+                        mbar_arrive_expect_tx(&bars.raw_full[st], 2 * kSbBytes);
+                        tma_2d(dst, it.expert < 0 ? &maps.sg : &maps.gate, sb * 144, y, &bars.raw_full[st]);
+                        tma_2d(dst + kSbBytes, it.expert < 0 ? &maps.su : &maps.up, sb * 144, y, &bars.raw_full[st]);
+                    } else {
+                        const int y = (it.expert < 0 ? 0 : it.expert * H) + it.mt * kTcRows;
+                        mbar_arrive_expect_tx(&bars.raw_full[st], kSbBytes);
+                        tma_2d(dst, it.expert < 0 ? &maps.sd : &maps.down, sb * 144, y, &bars.raw_full[st]);
+                    }
+                }
+                if (abort_flag) break;
             }
-            __syncwarp();
-            if (it.kind == kEnd || abort_flag) break;
+            // the last copies issued have landed before the CTA may exit
+            for (int k = max(0, gsb - kRawStages); k < gsb; k++)
+                wait_drain(&bars.raw_full[k % kRawStages], (k / kRawStages) & 1);
         }
-        if (lane == 0)  // the last copies issued have landed before the CTA may exit
-            for (int k = max(0, gsb - 2); k < gsb; k++) wait_drain(&bars.raw_full[k & 1], (k >> 1) & 1);
-    } else if (warp == 1) {
-        // ------------------------------------------------------ MMA issuer
+    } else if (warp == kMmaWarp || warp == kMma2Warp) {
+        // ------------------------------------------------------ MMA issuers
+        regs_dec();
+        // issuer mi: gate/up tiles -> matrix mi; down tiles -> chunks 2mi, 2mi+1
         if (lane == 0) {
+            const int mi = warp == kMmaWarp ? 0 : 1;
             int gsb = 0, gch = 0;
-            const uint32_t a_base = smem_u32(smem + kOffA), b_base = smem_u32(smem + kOffB);
+            const uint64_t b_desc0 = umma_desc(smem_u32(smem + kOffB), 128, 1024);
             for (int seq = 0;; seq++) {
                 const int slot = seq & 3;
                 if (!wait_phase(&bars.item_full[slot], (seq >> 2) & 1, &abort_flag, err)) break;
                 const Item it = items[slot];
                 if (it.kind == kEnd) break;
-                const int n_pad = (it.n + 15) & ~15, N = 2 * n_pad;
-                const uint32_t idesc = idesc_f16(kTcRows, N);
-                const int mats = it.kind == kGU ? 2 : 1;
-                const int nsb = it.kind == kGU ? gu_sb : dn_sb;
+                const int n_pad = (it.n + 15) & ~15;
+                const uint32_t idesc = idesc_f16(kTcRows, 2 * n_pad);
+                const bool gu = it.kind == kGU;
+                const int nsb = gu ? gu_sb : dn_sb;
                 bool ok = true;
                 for (int sb = 0; sb < nsb && ok; sb++, gsb++) {
                     const int db = gsb & 1;
                     if (gsb >= 2 && !(ok = wait_phase(&bars.d_empty[db], ((gsb >> 1) - 1) & 1, &abort_flag, err))) break;
                     tc_fence_after();
+                    const uint32_t d = tmem + (uint32_t)((db * 2 + mi) * kDCols);
                     for (int c = 0; c < 4; c++, gch++) {
-                        const int ab = gch & 1;
-                        if (!(ok = wait_phase(&bars.ab_full[ab], (gch >> 1) & 1, &abort_flag, err))) break;
-                        tc_fence_after();
-                        for (int s = 0; s < 4; s++) {
-                            const uint64_t bd = umma_desc(b_base + ab * kBBytes + 2 * s * 128, 128, 1024);
-                            for (int m = 0; m < mats; m++) {
-                                const uint64_t ad = umma_desc(a_base + (ab * 2 + m) * kABytes + 2 * s * 128, 128, 1024);
-                                mma_f16(tmem + (uint32_t)((db * 2 + m) * 128), ad, bd, idesc, (c | s) != 0);
-                            }
+                        const int ab = gch & 1, bs = gch % kBStages;
+                        if (!(ok = wait_phase(&bars.a_full[ab], (gch >> 1) & 1, &abort_flag, err))) break;
+                        if (!(ok = wait_phase(&bars.b_full[bs], (gch / kBStages) & 1, &abort_flag, err))) break;
+                        if (gu || (c >> 1) == mi) {
+                            tc_fence_after();
+                            const uint32_t ac = tmem + (uint32_t)(kACol0 + (ab * 2 + (gu ? mi : 0)) * 32);
+                            const uint64_t bd = b_desc0 + (uint64_t)((bs * kBBytes) >> 4);
+                            mma_ts(d, ac, bd, idesc, gu ? c != 0 : (c & 1) != 0);
+                            mma_ts1(d, ac + 8, bd + 16, idesc);
+                            mma_ts1(d, ac + 16, bd + 32, idesc);
+                            mma_ts1(d, ac + 24, bd + 48, idesc);
+                            mma_commit(&bars.a_empty[ab]);
+                            mma_commit(&bars.b_empty[bs]);
+                        } else {  // the other issuer's chunk: nothing read here
+                            arrive(&bars.a_empty[ab]);
+                            arrive(&bars.b_empty[bs]);
                         }
-                        mma_commit(&bars.ab_empty[ab]);
                     }
                     if (ok) mma_commit(&bars.d_full[db]);
                 }
@@ -379,13 +450,13 @@ __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a,
                 if (!ok) break;
             }
             // every MMA issued by this thread completes before TMEM is released
-            mma_commit(&bars.mma_done);
-            wait_drain(&bars.mma_done, 0);
+            mma_commit(&bars.mma_done[mi]);
+            wait_drain(&bars.mma_done[mi], 0);
         }
-    } else if (warp < kEpiWarp0) {
-        // ------------------------------------------------------ converters
+    } else if (warp == kStageWarp) {
+        // ------------------------------------------------------ B stager
+        regs_dec();
         grid_dep_wait();  // activations, routing and plan come from the preceding kernel
-        const int ct = tid - kConvWarp0 * 32;  // weight row of the tile
         int gsb = 0, gch = 0;
         for (int seq = 0;; seq++) {
             const int slot = seq & 3;
@@ -393,71 +464,136 @@ __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a,
             const Item it = items[slot];
             if (it.kind == kEnd) break;
             TokTab &tb = tabs[slot];
+            const bool gu = it.kind == kGU, sh = it.expert < 0;
             const int n_pad = (it.n + 15) & ~15, N = 2 * n_pad;
-            const int mats = it.kind == kGU ? 2 : 1;
-            const int nsb = it.kind == kGU ? gu_sb : dn_sb;
-            const int K = it.kind == kGU ? H : F;
-            const int ngroups = K / 32;
-            const __half *bsrc = it.kind == kGU ? a.x16 : a.mid16;
-            const float *gsums = it.kind == kGU ? a.xsum : a.msum;
-            if (it.kind == kDN) {
-                // the token tile's mid must be complete and converted (gu_done = gu_mt + 1)
-                if (ct == 0 && !wait_geq_int(a.gu_done + it.sub, gu_mt + 1, err)) abort_flag = 1;
-                bar_named(2, 128);
+            const int K = gu ? H : F;
+            for (int j = lane; j < n_pad; j += 32) {
+                const int jv = j < it.n ? j : 0;  // padding rows repeat token 0 (their columns are discarded)
+                const int sl = sh ? 0 : __ldcg(a.pairs + it.first + jv);
+                const int tok = sh ? it.tok0 + jv : sl / kTop;
+                const int mrow = sh ? T * kTop + it.tok0 + jv : it.first + jv;
+                tb.tok[j] = tok;
+                tb.mrow[j] = mrow;
+                tb.src[j] = gu ? tok * 2 * H : mrow * 2 * F;
+                tb.slot[j] = sl;
+                tb.w[j] = (sh || gu) ? 0.0f : __ldcg(a.wts + sl);
             }
-            if (ct < kTcTok)  // padding tokens get 0 so their (discarded) columns stay finite
-                tb.inv[ct] = ct >= it.n ? 0.0f : it.kind == kGU ? __ldcg(a.xinv + tb.tok[ct]) : __ldcg(a.midinv + tb.mrow[ct]);
-            const int grow = ct < it.n ? (it.kind == kGU ? tb.tok[ct] : tb.mrow[ct]) : 0;  // group-sum row
-            bar_named(2, 128);
-            bool ok = !abort_flag;
+            bool ok = true;
+            if (!gu) {  // the token tile's SwiGLU outputs: every gate/up tile of this sub-job has finished
+                if (lane == 0 && !wait_geq_int(a.gu_done + it.sub, gu_mt, err)) abort_flag = 1;
+                __syncwarp();
+                ok = !abort_flag;
+            }
+            __syncwarp();
+            if (lane == 0) arrive(&bars.tab_full[slot]);
+            const __half *bsrc = gu ? a.x16 : a.mid16;
+            const float *gsums = gu ? a.xsum : a.msum;
+            const int ngroups = K / 32;
+            const int nsb = gu ? gu_sb : dn_sb;
             for (int sb = 0; sb < nsb && ok; sb++, gsb++) {
-                const int st = gsb & 1, sc_slot = gsb & 3;
-                if (!(ok = wait_phase(&bars.raw_full[st], (gsb >> 1) & 1, &abort_flag, err))) break;
-                const unsigned char *raw = smem + kOffRaw + st * kRawStage;
+                const int sc_slot = gsb & 3;
                 if (gsb >= 4 && !(ok = wait_phase(&bars.sc_empty[sc_slot], ((gsb >> 2) - 1) & 1, &abort_flag, err)))
                     break;
+                // group sums and 1/s of this superblock's tokens (zero for padding), copied
+                // with the first chunk's B rows
                 unsigned char *scb = smem + kOffSc + sc_slot * kScSlot;
-                uint4 *scs = reinterpret_cast<uint4 *>(scb);
-                float *xs = reinterpret_cast<float *>(scb + kScRows);  // [8][64]
-                for (int m = 0; m < mats; m++) scs[m * kTcRows + ct] = q4k_row_scales(raw + m * kSbBytes + ct * 144);
-                if (ct < kTcTok) {
-                    float4 v0 = make_float4(0.f, 0.f, 0.f, 0.f), v1 = v0;
-                    if (ct < it.n) {
-                        const float4 *gp = reinterpret_cast<const float4 *>(gsums + (size_t)grow * ngroups + sb * 8);
-                        v0 = __ldcg(gp);
-                        v1 = __ldcg(gp + 1);
+                float *xs = reinterpret_cast<float *>(scb + kScRows);
+                float *inv2 = reinterpret_cast<float *>(scb + kScRows + kScXs);
+                for (int j = lane; j < n_pad; j += 32) {
+                    if (j < it.n) {
+                        const int grow = gu ? tb.tok[j] : tb.mrow[j];
+                        const float *gp = gsums + (size_t)grow * ngroups + sb * 8;
+                        cp_async16(xs + j * 8, gp);
+                        cp_async16(xs + j * 8 + 4, gp + 4);
+                        const float *ip = gu ? a.xinv + grow : a.midinv + (size_t)grow * gu_mt + 2 * sb;
+                        cp_async4(inv2 + j, ip);
+                        cp_async4(inv2 + kTcTok + j, gu ? ip : ip + 1);
+                    } else {
+                        reinterpret_cast<float4 *>(xs + j * 8)[0] = make_float4(0.f, 0.f, 0.f, 0.f);
+                        reinterpret_cast<float4 *>(xs + j * 8)[1] = make_float4(0.f, 0.f, 0.f, 0.f);
+                        inv2[j] = 0.0f;
+                        inv2[kTcTok + j] = 0.0f;
                     }
-                    xs[0 * kTcTok + ct] = v0.x, xs[1 * kTcTok + ct] = v0.y, xs[2 * kTcTok + ct] = v0.z;
-                    xs[3 * kTcTok + ct] = v0.w, xs[4 * kTcTok + ct] = v1.x, xs[5 * kTcTok + ct] = v1.y;
-                    xs[6 * kTcTok + ct] = v1.z, xs[7 * kTcTok + ct] = v1.w;
                 }
-                __syncwarp();
-                if (lane == 0) arrive(&bars.sc_full[sc_slot]);
+                // B rows of the four 64-value chunks: token j hi -> row j, lo -> row n_pad + j.
+                // Eight consecutive lanes fill the eight rows of one core matrix (128 B).
                 for (int c = 0; c < 4; c++, gch++) {
-                    const int ab = gch & 1;
-                    if (gch >= 2 && !(ok = wait_phase(&bars.ab_empty[ab], ((gch >> 1) - 1) & 1, &abort_flag, err)))
+                    const int bs = gch % kBStages;
+                    if (gch >= kBStages &&
+                        !(ok = wait_phase(&bars.b_empty[bs], (gch / kBStages - 1) & 1, &abort_flag, err)))
                         break;
-                    // B rows: token j hi -> row j, lo -> row n_pad + j; k-slots = values 64u .. 64u+63.
-                    // Eight consecutive threads fill the eight rows of one core matrix (128 B).
                     const int u = sb * 4 + c;
-                    unsigned char *bt = smem + kOffB + ab * kBBytes;
-                    for (int sgi = ct; sgi < N * 8; sgi += 128) {
+                    unsigned char *bt = smem + kOffB + bs * kBBytes;
+                    for (int sgi = lane; sgi < N * 8; sgi += 32) {
                         const int rr = sgi & 7, kb = (sgi >> 3) & 7, row = (sgi >> 6) * 8 + rr;
                         const int j = row < n_pad ? row : row - n_pad, hl = row < n_pad ? 0 : 1;
-                        unsigned char *dst = bt + ((row >> 3) * 8 + kb) * 128 + rr * 16;
-                        if (j < it.n)
-                            cp_async16(dst, bsrc + (size_t)tb.src[j] + hl * K + u * 64 + kb * 8);
-                        else
-                            *reinterpret_cast<uint4 *>(dst) = make_uint4(0, 0, 0, 0);
+                        cp_async16(bt + ((row >> 3) * 8 + kb) * 128 + rr * 16,
+                                   bsrc + (size_t)tb.src[j] + hl * K + u * 64 + kb * 8);
                     }
-                    for (int m = 0; m < mats; m++) {
-                        unsigned char *at = smem + kOffA + (ab * 2 + m) * kABytes + ((ct >> 3) * 8) * 128 + (ct & 7) * 16;
-                        q4k_unit_to_a(raw + m * kSbBytes + ct * 144, c, at, 128);
+                    cp_async_commit();
+                    if (c > 0) {  // the previous chunk (and with chunk 0 the group sums) has landed
+                        cp_async_wait_1();
+                        fence_proxy_async();
+                        __syncwarp();
+                        if (lane == 0) {
+                            arrive(&bars.b_full[(gch - 1) % kBStages]);
+                            if (c == 1) arrive(&bars.sc_full[sc_slot]);
+                        }
                     }
-                    cp_async_wait_all();
-                    fence_proxy_async();
+                }
+                if (!ok) break;
+                cp_async_wait_all();
+                fence_proxy_async();
+                __syncwarp();
+                if (lane == 0) arrive(&bars.b_full[(gch - 1) % kBStages]);
+            }
+            cp_async_wait_all();
+            __syncwarp();
+            if (lane == 0) arrive(&bars.item_empty[slot]);
+            if (!ok) break;
+        }
+        cp_async_wait_all();
+    } else if (warp >= kConvWarp0 && warp < kEpiWarp0) {
+        // ------------------------------------------------------ converters
+        regs_dec();
+        const int ct = 32 * (warp & 3) + lane;           // weight row of the tile = TMEM lane
+        const int nib = (warp - kConvWarp0) >> 2;        // 0: low nibbles + row scales, 1: high nibbles
+        const uint32_t a_lanes = tmem + ((uint32_t)(32 * (warp & 3)) << 16) + kACol0 + nib * 16;
+        int gsb = 0, gch = 0;
+        for (int seq = 0;; seq++) {
+            const int slot = seq & 3;
+            if (!wait_phase(&bars.item_full[slot], (seq >> 2) & 1, &abort_flag, err)) break;
+            const Item it = items[slot];
+            if (it.kind == kEnd) break;
+            const int mats = it.kind == kGU ? 2 : 1;
+            const int nsb = it.kind == kGU ? gu_sb : dn_sb;
+            bool ok = true;
+            for (int sb = 0; sb < nsb && ok; sb++, gsb++) {
+                const int st = gsb % kRawStages, sc_slot = gsb & 3;
+                if (!(ok = wait_phase(&bars.raw_full[st], (gsb / kRawStages) & 1, &abort_flag, err))) break;
+                const unsigned char *raw = smem + kOffRaw + st * kRawStage;
+                if (nib == 0) {
+                    if (gsb >= 4 && !(ok = wait_phase(&bars.sc_empty[sc_slot], ((gsb >> 2) - 1) & 1, &abort_flag, err)))
+                        break;
+                    uint4 *scs = reinterpret_cast<uint4 *>(smem + kOffSc + sc_slot * kScSlot);
+                    for (int m = 0; m < mats; m++) scs[m * kTcRows + ct] = q4k_row_scales(raw + m * kSbBytes + ct * 144);
                     __syncwarp();
-                    if (lane == 0) arrive(&bars.ab_full[ab]);
+                    if (lane == 0) arrive(&bars.sc_full[sc_slot]);
+                }
+                for (int c = 0; c < 4; c++, gch++) {
+                    const int ab = gch & 1;
+                    if (gch >= 2 && !(ok = wait_phase(&bars.a_empty[ab], ((gch >> 1) - 1) & 1, &abort_flag, err)))
+                        break;
+                    tc_fence_after();
+                    for (int m = 0; m < mats; m++) {
+                        uint32_t r[16];
+                        q4k_half_cols(raw + m * kSbBytes + ct * 144, c, nib, r);
+                        tmem_st16(a_lanes + (uint32_t)((ab * 2 + m) * 32), r);
+                    }
+                    tmem_wait_st();
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) arrive(&bars.a_full[ab]);
                 }
                 __syncwarp();
                 if (lane == 0) arrive(&bars.raw_empty[st]);
@@ -466,31 +602,32 @@ __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a,
             if (lane == 0) arrive(&bars.item_empty[slot]);
             if (!ok) break;
         }
-    } else {
+    } else if (warp >= kEpiWarp0) {
         // ------------------------------------------------------ epilogue
+        regs_inc();
         grid_dep_wait();
         const int ew = warp - kEpiWarp0;         // 0..7
         const int q = warp & 3;                  // TMEM lane quarter
         const int r = 32 * q + lane;             // row within the tile
         const int half = ew >> 2;                // token half
         const int et = tid - kEpiWarp0 * 32;     // 0..255
+        constexpr int kHalf = kTcTok / 2;        // tokens per half, at most
         int gsb = 0;
         for (int seq = 0;; seq++) {
             const int slot = seq & 3;
-            if (!wait_phase(&bars.item_full[slot], (seq >> 2) & 1, &abort_flag, err)) break;
+            bool ok = wait_phase(&bars.item_full[slot], (seq >> 2) & 1, &abort_flag, err);
             const Item it = items[slot];
-            if (it.kind == kEnd) break;
+            if (!bar_all(3, 256, ok) || it.kind == kEnd) break;
             const TokTab &tb = tabs[slot];
             const int n_pad = (it.n + 15) & ~15, hw = n_pad >> 1;  // tokens per half (multiple of 8)
             const int j0 = half * hw;
-            const int mats = it.kind == kGU ? 2 : 1;
-            const int nsb = it.kind == kGU ? gu_sb : dn_sb;
-            float2 acc[2][16];
+            const bool gu = it.kind == kGU;
+            const int nsb = gu ? gu_sb : dn_sb;
+            float2 acc[2][kHalf / 2];
 #pragma unroll
             for (int m = 0; m < 2; m++)
 #pragma unroll
-                for (int p = 0; p < 16; p++) acc[m][p] = make_float2(0.0f, 0.0f);
-            bool ok = true;
+                for (int p = 0; p < kHalf / 2; p++) acc[m][p] = make_float2(0.0f, 0.0f);
             for (int sb = 0; sb < nsb && ok; sb++, gsb++) {
                 const int db = gsb & 1, sc_slot = gsb & 3;
                 if (!(ok = wait_phase(&bars.d_full[db], (gsb >> 1) & 1, &abort_flag, err))) break;
@@ -499,37 +636,67 @@ __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a,
                 const unsigned char *scb = smem + kOffSc + sc_slot * kScSlot;
                 const uint4 *scs = reinterpret_cast<const uint4 *>(scb);
                 const float *xs = reinterpret_cast<const float *>(scb + kScRows);
+                const float *inv2 = reinterpret_cast<const float *>(scb + kScRows + kScXs);
+                const uint32_t lanes = tmem + ((uint32_t)(32 * q) << 16);
+                const float2 k2048 = make_float2(1.0f / 2048.0f, 1.0f / 2048.0f);
+                if (gu) {
 #pragma unroll
-                for (int m = 0; m < 2; m++) {
-                    if (m >= mats) break;
-                    const uint4 sv = scs[m * kTcRows + r];
+                    for (int m = 0; m < 2; m++) {
+                        const uint4 sv = scs[m * kTcRows + r];
+                        const float2 d2 = make_float2(__uint_as_float(sv.x), __uint_as_float(sv.x));
+                        const float2 nm2 = make_float2(-__uint_as_float(sv.y), -__uint_as_float(sv.y));
+                        float mg[8];
+#pragma unroll
+                        for (int g = 0; g < 8; g++) mg[g] = (float)(((g < 4 ? sv.z : sv.w) >> (8 * (g & 3))) & 0xFFu);
+                        const uint32_t col0 = lanes + (uint32_t)((db * 2 + m) * kDCols);
+#pragma unroll
+                        for (int cb = 0; cb < kHalf / 8; cb++) {
+                            if (cb * 8 >= hw) break;
+                            uint32_t rh[8], rl[8];
+                            tmem_ld8_nw(col0 + j0 + cb * 8, rh);
+                            tmem_ld8_nw(col0 + n_pad + j0 + cb * 8, rl);
+                            tmem_wait_ld();
+#pragma unroll
+                            for (int pp = 0; pp < 4; pp++) {
+                                const int j = j0 + cb * 8 + 2 * pp;
+                                const float2 hi = make_float2(__uint_as_float(rh[2 * pp]), __uint_as_float(rh[2 * pp + 1]));
+                                const float2 lo = make_float2(__uint_as_float(rl[2 * pp]), __uint_as_float(rl[2 * pp + 1]));
+                                const float2 inv = *reinterpret_cast<const float2 *>(&inv2[j]);
+                                const float2 dot = __fmul2_rn(__ffma2_rn(lo, k2048, hi), inv);
+                                const float2 mt = mterm2(mg, xs, j);
+                                float2 &ac = acc[m][cb * 4 + pp];
+                                ac = __ffma2_rn(d2, dot, ac);
+                                ac = __ffma2_rn(nm2, mt, ac);
+                            }
+                        }
+                    }
+                } else {
+                    const uint4 sv = scs[r];
                     const float2 d2 = make_float2(__uint_as_float(sv.x), __uint_as_float(sv.x));
                     const float2 nm2 = make_float2(-__uint_as_float(sv.y), -__uint_as_float(sv.y));
                     float mg[8];
 #pragma unroll
                     for (int g = 0; g < 8; g++) mg[g] = (float)(((g < 4 ? sv.z : sv.w) >> (8 * (g & 3))) & 0xFFu);
-                    const uint32_t col0 = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)((db * 2 + m) * 128);
+                    const uint32_t c0 = lanes + (uint32_t)((db * 2) * kDCols);
 #pragma unroll
-                    for (int cb = 0; cb < 4; cb++) {
+                    for (int cb = 0; cb < kHalf / 8; cb++) {
                         if (cb * 8 >= hw) break;
-                        uint32_t rh[8], rl[8];
-                        tmem_ld8_nw(col0 + j0 + cb * 8, rh);
-                        tmem_ld8_nw(col0 + n_pad + j0 + cb * 8, rl);
-                        tmem_wait_ld();
 #pragma unroll
-                        for (int pp = 0; pp < 4; pp++) {
-                            const int j = j0 + cb * 8 + 2 * pp;
-                            const float2 hi = make_float2(__uint_as_float(rh[2 * pp]), __uint_as_float(rh[2 * pp + 1]));
-                            const float2 lo = make_float2(__uint_as_float(rl[2 * pp]), __uint_as_float(rl[2 * pp + 1]));
-                            const float2 inv = *reinterpret_cast<const float2 *>(&tb.inv[j]);
-                            const float2 dot = __fmul2_rn(__ffma2_rn(lo, make_float2(1.0f / 2048.0f, 1.0f / 2048.0f), hi), inv);
-                            float2 mt = make_float2(0.0f, 0.0f);
+                        for (int h = 0; h < 2; h++) {  // the two 128-value halves, one B scale each
+                            uint32_t rh[8], rl[8];
+                            tmem_ld8_nw(c0 + h * kDCols + j0 + cb * 8, rh);
+                            tmem_ld8_nw(c0 + h * kDCols + n_pad + j0 + cb * 8, rl);
+                            tmem_wait_ld();
 #pragma unroll
-                            for (int g = 0; g < 8; g++)
-                                mt = __ffma2_rn(make_float2(mg[g], mg[g]), *reinterpret_cast<const float2 *>(&xs[g * kTcTok + j]), mt);
-                            float2 &ac = acc[m][cb * 4 + pp];
-                            ac = __ffma2_rn(d2, dot, ac);
-                            ac = __ffma2_rn(nm2, mt, ac);
+                            for (int pp = 0; pp < 4; pp++) {
+                                const int j = j0 + cb * 8 + 2 * pp;
+                                const float2 v = __ffma2_rn(make_float2(__uint_as_float(rl[2 * pp]), __uint_as_float(rl[2 * pp + 1])), k2048,
+                                                            make_float2(__uint_as_float(rh[2 * pp]), __uint_as_float(rh[2 * pp + 1])));
+                                const float2 dot = __fmul2_rn(v, *reinterpret_cast<const float2 *>(&inv2[h * kTcTok + j]));
+                                float2 &ac = acc[0][cb * 4 + pp];
+                                ac = __ffma2_rn(d2, dot, ac);
+                                if (h) ac = __ffma2_rn(nm2, mterm2(mg, xs, j), ac);
+                            }
                         }
                     }
                 }
@@ -540,110 +707,115 @@ __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a,
                     arrive(&bars.sc_empty[sc_slot]);
                 }
             }
-            if (ok) {
-                if (it.kind == kGU) {
+            ok = ok && wait_phase(&bars.tab_full[slot], (seq >> 2) & 1, &abort_flag, err);
+            if (!bar_all(3, 256, ok)) break;
+            // the tile's outputs (SwiGLU for gate/up) to the shared buffer sv[token][row]
+            float *sv = reinterpret_cast<float *>(smem + kOffV);
 #pragma unroll
-                    for (int p = 0; p < 16; p++) {
+            for (int cb = 0; cb < kHalf / 8; cb++) {
+                if (cb * 8 < hw) {
 #pragma unroll
-                        for (int e = 0; e < 2; e++) {
-                            const int jj = 2 * p + e, j = j0 + jj;
-                            if (jj < hw && j < it.n) {
-                                const float g = e ? acc[0][p].y : acc[0][p].x, uu = e ? acc[1][p].y : acc[1][p].x;
-                                a.mid[(size_t)tb.mrow[j] * F + it.mt * kTcRows + r] = (g * sigmoidf_ref(g)) * uu;
-                            }
+                    for (int pp = 0; pp < 4; pp++) {
+                        float2 v = acc[0][cb * 4 + pp];
+                        if (gu) {
+                            const float2 u = acc[1][cb * 4 + pp];
+                            v.x = (v.x * sigmoidf_ref(v.x)) * u.x;
+                            v.y = (v.y * sigmoidf_ref(v.y)) * u.y;
                         }
+                        const int j = j0 + cb * 8 + 2 * pp;
+                        sv[j * kTcRows + r] = v.x;
+                        sv[(j + 1) * kTcRows + r] = v.y;
                     }
+                }
+            }
+            bar_named(3, 256);
+            const int rr = et & 127;  // row handled by this thread in the per-token loops
+            if (gu) {
+                // per token (one warp each): the four 32-row group sums and a power-of-two
+                // scale from the tile's max |v|
+#pragma unroll 1
+                for (int j = ew; j < it.n; j += kEpiWarps) {
+                    const float *vj = sv + j * kTcRows;
+                    const float v0 = vj[lane], v1 = vj[32 + lane], v2 = vj[64 + lane], v3 = vj[96 + lane];
+                    float s0 = v0, s1 = v1, s2 = v2, s3 = v3;
+#pragma unroll
+                    for (int dd = 16; dd; dd >>= 1) {
+                        s0 += __shfl_xor_sync(0xffffffffu, s0, dd);
+                        s1 += __shfl_xor_sync(0xffffffffu, s1, dd);
+                        s2 += __shfl_xor_sync(0xffffffffu, s2, dd);
+                        s3 += __shfl_xor_sync(0xffffffffu, s3, dd);
+                    }
+                    const float mx = fmaxf(fmaxf(fabsf(v0), fabsf(v1)), fmaxf(fabsf(v2), fabsf(v3)));
+                    const uint32_t mb = __reduce_max_sync(0xffffffffu, __float_as_uint(mx));
+                    if (lane == 0) {
+                        float sc, inv;
+                        pow2_scale(__uint_as_float(mb), sc, inv);
+                        const size_t mrow = (size_t)tb.mrow[j];
+                        *reinterpret_cast<float4 *>(a.msum + mrow * (F / 32) + it.mt * 4) = make_float4(s0, s1, s2, s3);
+                        a.midinv[mrow * gu_mt + it.mt] = inv;
+                        s_scale[j] = sc;
+                    }
+                }
+                bar_named(3, 256);
+                // fp16 hi/lo split of v*s for the down tiles
+#pragma unroll 1
+                for (int j = et >> 7; j < it.n; j += 2) {
+                    const float v = sv[j * kTcRows + rr] * s_scale[j];
+                    const __half hi = __float2half_rn(v);
+                    const size_t base = (size_t)tb.mrow[j] * 2 * F + it.mt * kTcRows + rr;
+                    a.mid16[base] = hi;
+                    a.mid16[base + F] = __float2half_rn((v - __half2float(hi)) * 2048.0f);
+                }
+                __threadfence();
+                bar_named(3, 256);
+                if (et == 0) atomicAdd(a.gu_done + it.sub, 1);
+            } else {
+                const int row = it.mt * kTcRows + rr;
+#pragma unroll 1
+                for (int j = et >> 7; j < it.n; j += 2) {
+                    const float y = sv[j * kTcRows + rr];
+                    if (it.expert < 0) a.shout[(size_t)tb.tok[j] * H + row] = y;
+                    else a.slots[(size_t)tb.slot[j] * H + row] = y * tb.w[j];
+                }
+                __threadfence();
+                bar_named(3, 256);
+                if (et == 0) s_ncombine = 0;
+                bar_named(3, 256);
+                if (et < it.n) {
+                    const int t = tb.tok[et];
+                    int *cnt = a.tilecnt + (size_t)t * dn_mt + it.mt;
+                    const int expect = __ldcg(a.expect + t) & 0xffff;
+                    if (atomicAdd(cnt, 1) == expect - 1) {
+                        *cnt = 0;
+                        s_combine[atomicAdd(&s_ncombine, 1)] = t;
+                    }
+                }
+                bar_named(3, 256);
+                const int nc = s_ncombine;
+                if (nc) {
                     __threadfence();
-                    bar_named(3, 256);
-                    if (et == 0) s_flag = atomicAdd(a.gu_done + it.sub, 1) == gu_mt - 1;
-                    bar_named(3, 256);
-                    if (s_flag) {
-                        // last gate/up tile of this token tile: fp16 hi/lo copies of its mid rows
-                        __threadfence();
-                        for (int j = ew; j < it.n; j += 8) {
-                            const size_t mrow = (size_t)tb.mrow[j];
-                            const float *src = a.mid + mrow * F;
-                            float mx = 0.0f;
-                            for (int i = lane; i < F; i += 32) mx = fmaxf(mx, fabsf(__ldcg(src + i)));
+                    for (int ci = et >> 7; ci < nc; ci += 2) {
+                        const int t = s_combine[ci];
+                        const int rr = it.mt * kTcRows + (et & 127);
+                        const bool bad = (__ldcg(a.expect + t) & (int)kBad) != 0;
+                        float sum = 0.0f;
 #pragma unroll
-                            for (int dd = 16; dd; dd >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, dd));
-                            int e = 0;
-                            if (mx > 0.0f && isfinite(mx)) frexpf(mx, &e);
-                            const float s = (mx > 0.0f && isfinite(mx)) ? ldexpf(1.0f, 14 - e) : 1.0f;
-                            __half *dst = a.mid16 + mrow * 2 * F;
-                            for (int i = lane; i < F; i += 32) {
-                                const float v = __ldcg(src + i) * s;
-                                const __half hi = __float2half_rn(v);
-                                dst[i] = hi;
-                                dst[F + i] = __float2half_rn((v - __half2float(hi)) * 2048.0f);
-                            }
-                            for (int g = 0; g < F / 32; g++) {
-                                float v = __ldcg(src + g * 32 + lane);
-#pragma unroll
-                                for (int dd = 16; dd; dd >>= 1) v += __shfl_xor_sync(0xffffffffu, v, dd);
-                                if (lane == 0) a.msum[mrow * (F / 32) + g] = v;
-                            }
-                            if (lane == 0) a.midinv[mrow] = 1.0f / s;
+                        for (int k = 0; k < kTop; k++) {
+                            const int id = __ldcg(a.ids + t * kTop + k);
+                            sum += id >= 0 ? __ldcg(a.slots + ((size_t)t * kTop + k) * H + rr) : 0.0f;
                         }
-                        __threadfence();
-                        bar_named(3, 256);
-                        if (et == 0) atomicAdd(a.gu_done + it.sub, 1);
-                    }
-                } else {
-                    const int row = it.mt * kTcRows + r;
-#pragma unroll
-                    for (int p = 0; p < 16; p++) {
-#pragma unroll
-                        for (int e = 0; e < 2; e++) {
-                            const int jj = 2 * p + e, j = j0 + jj;
-                            if (jj < hw && j < it.n) {
-                                const float y = e ? acc[0][p].y : acc[0][p].x;
-                                if (it.expert < 0) a.shout[(size_t)tb.tok[j] * H + row] = y;
-                                else a.slots[(size_t)tb.slot[j] * H + row] = y * tb.w[j];
-                            }
-                        }
-                    }
-                    __threadfence();
-                    bar_named(3, 256);
-                    if (et == 0) s_ncombine = 0;
-                    bar_named(3, 256);
-                    if (et < it.n) {
-                        const int t = tb.tok[et];
-                        int *cnt = a.tilecnt + (size_t)t * dn_mt + it.mt;
-                        const int expect = __ldcg(a.expect + t) & 0xffff;
-                        if (atomicAdd(cnt, 1) == expect - 1) {
-                            *cnt = 0;
-                            s_combine[atomicAdd(&s_ncombine, 1)] = t;
-                        }
-                    }
-                    bar_named(3, 256);
-                    const int nc = s_ncombine;
-                    if (nc) {
-                        __threadfence();
-                        for (int ci = et >> 7; ci < nc; ci += 2) {
-                            const int t = s_combine[ci];
-                            const int rr = it.mt * kTcRows + (et & 127);
-                            const bool bad = (__ldcg(a.expect + t) & (int)kBad) != 0;
-                            float sum = 0.0f;
-#pragma unroll
-                            for (int k = 0; k < kTop; k++) {
-                                const int id = __ldcg(a.ids + t * kTop + k);
-                                sum += id >= 0 ? __ldcg(a.slots + ((size_t)t * kTop + k) * H + rr) : 0.0f;
-                            }
-                            if (a.sg) sum = __fmaf_rn(__ldcg(a.shout + (size_t)t * H + rr), sigmoidf_ref(__ldcg(a.sgate + t)), sum);
-                            a.out[(size_t)t * H + rr] = bad ? __int_as_float(0x7fc00000) : sum;
-                        }
+                        if (a.sg) sum = __fmaf_rn(__ldcg(a.shout + (size_t)t * H + rr), sigmoidf_ref(__ldcg(a.sgate + t)), sum);
+                        a.out[(size_t)t * H + rr] = bad ? __int_as_float(0x7fc00000) : sum;
                     }
                 }
             }
             __syncwarp();
             if (lane == 0) arrive(&bars.item_empty[slot]);
-            if (!ok) break;
         }
     }
     // ---------------------------------------------------------- teardown
     __syncthreads();
-    if (warp == 1) {
+    if (warp == kMmaWarp) {
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem));
     }

@@ -5,7 +5,7 @@
 
 namespace nb {
 
-constexpr int kTcTok = 64;     // tokens per sub-job (token tile of one expert)
+constexpr int kTcTok = 48;     // tokens per sub-job (token tile of one expert)
 constexpr int kTcRows = 128;   // weight rows per tile (MMA M)
 
 // One token tile of one expert. expert < 0 is the shared expert, whose tokens
@@ -29,15 +29,16 @@ struct TcArgs {
     const int *ids;        // [T*10]
     const int *expect;     // [T]: contributions per token (| bad bit)
     const float *sgate;    // [T] shared-gate logits, or null
-    float *mid;            // [(T*10+T)][F] fp32: routed pair p -> row p, shared token t -> row T*10+t
-    __half *mid16;         // [(T*10+T)][2][F]
-    float *midinv, *msum;  // [(T*10+T)], [(T*10+T)][F/32]
+    // SwiGLU outputs, one row per routed pair p (row p) and shared token t (row T*10+t):
+    __half *mid16;         // [rows][2][F]: v*s hi, (v*s - hi)*2048 lo, s per 128-value tile
+    float *midinv;         // [rows][F/128]: 1/s
+    float *msum;           // [rows][F/32]: 32-value group sums of v
     float *slots;          // [T*10][H]
     float *shout;          // [T][H]
     float *out;            // [T][H]
     int *queue;            // zero between calls (reset by the kernel's last CTA)
     int *tc_ticket;        // zero between calls
-    int *gu_done;          // [n_sub], zeroed by the planner
+    int *gu_done;          // [n_sub] finished gate/up tiles, zeroed by the planner
     int *tilecnt;          // [T][H/128], zeroed by the planner
     int *err;
 };
@@ -53,6 +54,19 @@ int tc_launch(const TcArgs &a, const TcMaps &m, cudaStream_t st, bool pdl);
 // x16 / xinv / xsum for T tokens (one CTA per token)
 int tc_prep_launch(const float *x, int T, int H, __half *x16, float *xinv, float *xsum, cudaStream_t st);
 
+// Power of two s with max|v*s| in [2^13, 2^14) for mx = max|v| (s = 1 when
+// mx is zero, subnormal-small or not finite), and 1/s, both built from the
+// exponent bits.
+__device__ __forceinline__ void pow2_scale(float mx, float &s, float &inv) {
+    const int E = (int)((__float_as_uint(mx) >> 23) & 0xFF);  // mx in [2^(E-127), 2^(E-126))
+    if (E >= 14 && E <= 254) {
+        s = __uint_as_float((uint32_t)(267 - E) << 23);  // 2^(140-E)
+        inv = __uint_as_float((uint32_t)(E - 13) << 23);  // 2^(E-140)
+    } else {
+        s = inv = 1.0f;
+    }
+}
+
 // Per-token preparation shared by the decode router kernel and the prep kernel:
 // scale to max|x*s| in [2^13, 2^14), split into fp16 hi/lo, 32-value group sums.
 __device__ inline void tc_prep_token(const float *x, int H, __half *x16, float *xinv, float *xsum) {
@@ -67,10 +81,9 @@ __device__ inline void tc_prep_token(const float *x, int H, __half *x16, float *
     m = 0.0f;
     for (int w = 0; w < nw; w++) m = fmaxf(m, red[w]);
     __syncthreads();
-    int e = 0;
-    if (m > 0.0f && isfinite(m)) frexpf(m, &e);  // m = f * 2^e, f in [0.5, 1)
-    const float s = (m > 0.0f && isfinite(m)) ? ldexpf(1.0f, 14 - e) : 1.0f;
-    if (tid == 0) *xinv = 1.0f / s;
+    float s, inv;
+    pow2_scale(m, s, inv);
+    if (tid == 0) *xinv = inv;
     for (int i = tid; i < H; i += blockDim.x) {
         const float v = x[i] * s;
         const __half hi = __float2half_rn(v);
