@@ -126,13 +126,15 @@ Layout layout(int T, int H, int F) {
     L.mid = take(sizeof(float) * ((size_t)T * kTop + T) * F);
     L.slots = take(sizeof(float) * (size_t)T * kTop * H);
     L.shared = take(sizeof(float) * (size_t)T * H);
-    L.x16 = take(sizeof(__half) * (size_t)T * 2 * H);
-    L.xinv = take(sizeof(float) * (size_t)T);
-    L.xsum = take(sizeof(float) * (size_t)T * (H / 32));
+    // tensor-core gate/up activations: per token (T <= one token tile) or per routed row
+    const size_t rows = (size_t)T * kTop + T;
+    L.x16 = take(sizeof(__half) * rows * 2 * H);
+    L.xinv = take(sizeof(float) * rows * 4);
+    L.xsum = take(sizeof(float) * rows * (H / 32));
     L.sub = take(sizeof(SubJob) * (size_t)max_subjobs(T));
     L.nsub = take(sizeof(int));
     L.mid16 = take(sizeof(__half) * ((size_t)T * kTop + T) * 2 * F);
-    L.midinv = take(sizeof(float) * ((size_t)T * kTop + T) * (F / 128));
+    L.midinv = take(sizeof(float) * rows * (((F / 128) + 3) & ~3));
     L.msum = take(sizeof(float) * ((size_t)T * kTop + T) * (F / 32));
     L.gudone = take(sizeof(int) * (size_t)max_subjobs(T));
     L.tilecnt = take(sizeof(int) * (size_t)T * (H / kTcRows));
@@ -895,9 +897,11 @@ int run_experts(float *out, const float *x, const int *ids, const float *wts, in
         t.sg = static_cast<const unsigned char *>(sg), t.su = static_cast<const unsigned char *>(su);
         t.sd = static_cast<const unsigned char *>(sd);
         t.grb = grb, t.drb = drb;
+        t.all_tok = T <= kTcTok;
         t.x16 = reinterpret_cast<__half *>(base + L.x16);
         t.xinv = reinterpret_cast<float *>(base + L.xinv);
         t.xsum = reinterpret_cast<float *>(base + L.xsum);
+        t.mi_stride = ((F / 128) + 3) & ~3;
         t.sub = reinterpret_cast<SubJob *>(base + L.sub);
         t.n_sub = reinterpret_cast<int *>(base + L.nsub);
         t.shared_subs = has_shared ? (T + kTcTok - 1) / kTcTok : 0;
@@ -914,19 +918,22 @@ int run_experts(float *out, const float *x, const int *ids, const float *wts, in
         t.tilecnt = reinterpret_cast<int *>(base + L.tilecnt);
         t.err = &pl.hdr->error;
         TcMaps maps;
-        if (int rc = tc_make_maps(t, maps)) return rc;
+        if (int rc = tc_make_maps(t, maps, kTcTok)) return rc;
         {
             Span sp(kPlan, st);
             tc_plan_kernel<<<1, 1024, 0, st>>>(pl, ids, T, H, has_shared ? 1 : 0, const_cast<SubJob *>(t.sub),
                                                const_cast<int *>(t.n_sub), const_cast<int *>(t.expect), t.gu_done,
                                                t.tilecnt, out);
             if (int rc = cudaGetLastError()) return rc;
-            if (int rc = tc_prep_launch(x, T, H, const_cast<__half *>(t.x16), const_cast<float *>(t.xinv),
-                                        const_cast<float *>(t.xsum), st))
-                return rc;
+            const int rc = t.all_tok ? tc_prep_launch(x, T, H, const_cast<__half *>(t.x16), const_cast<float *>(t.xinv),
+                                                      const_cast<float *>(t.xsum), st)
+                                     : tc_prep_rows_launch(x, T, H, pl.pairs, &pl.hdr->n_pairs, has_shared,
+                                                           const_cast<__half *>(t.x16), const_cast<float *>(t.xinv),
+                                                           const_cast<float *>(t.xsum), st);
+            if (rc) return rc;
         }
         Span sp(kExpertsFused, st);
-        return tc_launch(t, maps, st, false);
+        return tc_launch(t, maps, st, false, kTcTok);
     }
 
     GateUpArgs ga{x, T, H, F, static_cast<const unsigned char *>(gate), static_cast<const unsigned char *>(up),

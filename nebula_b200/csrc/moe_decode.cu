@@ -154,7 +154,7 @@ __global__ void __launch_bounds__(128) dec_router_kernel(DecArgs a) {
             const int t = blockIdx.x;
             const float *src = xs + (size_t)t * H;
             if (a.use_tc) {
-                tc_prep_token(src, H, a.x16 + (size_t)t * 2 * H, a.xinv + t, a.xsum + (size_t)t * (H / 32));
+                tc_prep_token(src, H, a.x16 + (size_t)t * 2 * H, a.xinv + (size_t)t * 4, a.xsum + (size_t)t * (H / 32));
             } else {
                 float *dst = a.xpair + (size_t)t * H;
                 for (int i = tid; i < H; i += blockDim.x) dst[(i >> 6) * 64 + pair_pos<QG>(i & 63)] = src[i];
@@ -796,11 +796,11 @@ DecLayout dec_layout(int T, int H, int F) {
     L.slots = take(sizeof(float) * T * kTop * H);
     L.shout = take(sizeof(float) * T * H);
     L.x16 = take(sizeof(__half) * T * 2 * H);
-    L.xinv = take(sizeof(float) * T);
+    L.xinv = take(sizeof(float) * T * 4);
     L.sub = take(sizeof(SubJob) * (kExperts + 1));
     L.nsub = take(sizeof(int));
     L.mid16 = take(sizeof(__half) * (T * kTop + T) * 2 * F);
-    L.midinv = take(sizeof(float) * (T * kTop + T) * (F / 128));
+    L.midinv = take(sizeof(float) * (T * kTop + T) * (((F / 128) + 3) & ~3));
     L.total = p;
     return L;
 }
@@ -853,7 +853,9 @@ int dec_run(const DecArgs &in, cudaStream_t st, cudaEvent_t split) {
         t.T = a.T, t.H = a.H, t.F = a.F;
         t.gate = a.gate, t.up = a.up, t.down = a.down, t.sg = a.sg, t.su = a.su, t.sd = a.sd;
         t.grb = a.grb, t.drb = a.drb;
+        t.all_tok = 1;
         t.x16 = a.x16, t.xinv = a.xinv, t.xsum = a.xsum;
+        t.mi_stride = ((a.F / 128) + 3) & ~3;
         t.sub = a.sub, t.n_sub = a.n_sub, t.shared_subs = a.sg ? 1 : 0;
         t.pairs = a.pairs, t.wts = a.wts, t.ids = a.ids, t.expect = a.expect, t.sgate = a.sg ? a.sgate : nullptr;
         t.mid16 = a.mid16, t.midinv = a.midinv, t.msum = a.msum;
@@ -861,8 +863,8 @@ int dec_run(const DecArgs &in, cudaStream_t st, cudaEvent_t split) {
         t.queue = &a.ctr->tc_queue, t.tc_ticket = &a.ctr->tc_ticket;
         t.gu_done = a.ctr->gu_done, t.tilecnt = a.ctr->tilecnt, t.err = &a.hdr->error;
         TcMaps maps;
-        if ((rc = tc_make_maps(t, maps))) return rc;
-        return tc_launch(t, maps, st, pdl);
+        if ((rc = tc_make_maps(t, maps, kMaxDecodeTokens))) return rc;
+        return tc_launch(t, maps, st, pdl, kMaxDecodeTokens);
     }
     const int ctas = sm_count();
     if (a.QG == 12 && a.QD == 12) return launch_k2<12, 12>(a, st, ctas, pdl);

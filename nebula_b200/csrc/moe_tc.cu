@@ -10,7 +10,7 @@
 //                     bytes by four converter warps straight into tensor
 //                     memory (tcgen05.st; lane = weight row), so A never
 //                     crosses shared memory;
-//   B = [v_hi | v_lo] fp16 in shared memory (UMMA K-major, no swizzle),
+//   B = [v_hi | v_lo] fp16 in shared memory (UMMA K-major, 128B swizzle),
 //                     v*s = v_hi + v_lo/2048 with a power of two s (22-bit
 //                     precision): the token's activations (one s per token)
 //                     for gate/up, the SwiGLU output (one s per token and
@@ -30,8 +30,9 @@
 // (qwen/cpu.c:209-231, qwen/gpu.cu:552).
 //
 // Raw weight bytes stream with 2-D TMA tensor copies (a 144-byte x 128-row
-// box = one superblock of 128 rows) into a three-stage ring; B rows stream
-// with cp.async into a three-stage ring run ahead by their own warp. Roles:
+// box = one superblock of 128 rows) into a three-stage ring; B rows (128B
+// swizzled, hi rows then lo rows), group sums and scales stream with 2-D TMA
+// copies issued by their own warp into four- and four-slot rings. Roles:
 //   warp 0 lane 0   producer: claims items, issues TMA
 //   warp 1          TMEM owner; lane 0 issues the gate (first-half) MMAs
 //   warp 2          B stager: token table, B rows, per-superblock group sums
@@ -63,20 +64,30 @@ static_assert(kEpiWarp0 % 4 == 0 && kEpiWarps % 4 == 0, "register split is per w
 constexpr int kSbBytes = kTcRows * 144;           // one superblock of 128 Q4_K rows
 constexpr int kRawStage = 2 * kSbBytes;           // gate + up
 constexpr int kRawStages = 3;
-constexpr int kBBytes = 2 * kTcTok * 64 * 2;      // up to 96 B rows x 64 halves
+constexpr int kOffRaw = 0;
 constexpr int kBStages = 4;
 constexpr int kScRows = 2 * kTcRows * 16;         // d, dmin, m[8] per row per matrix
-constexpr int kScXs = 8 * kTcTok * 4;             // the superblock's 8 group sums per token [token][8]
-constexpr int kScSlot = kScRows + kScXs + 2 * kTcTok * 4;  // + 1/s per token per 128-value half
-constexpr int kVBytes = kTcTok * kTcRows * 4;     // one tile's per-token outputs [token][row]
-constexpr int kOffRaw = 0, kOffB = kOffRaw + kRawStages * kRawStage, kOffSc = kOffB + kBStages * kBBytes,
-              kOffV = kOffSc + 4 * kScSlot, kSmem = kOffV + kVBytes;
-// Tensor memory (512 columns): D[db][m] at (db*2+m)*kDCols, A[ab][m] (32
-// columns = 64 fp16 of one 64-value chunk) at kACol0 + (ab*2+m)*32.
-constexpr int kDCols = 2 * kTcTok;
-constexpr int kACol0 = 4 * kDCols;
-static_assert(kACol0 + 4 * 32 <= 512, "tensor memory budget");
-static_assert(kSmem % 16 == 0 && kScSlot % 16 == 0, "alignment");
+// Layout of one instantiation for token tiles of up to TOK tokens.
+template <int TOK>
+struct Cfg {
+    static constexpr int kBBytes = 2 * TOK * 128;             // B: TOK hi rows, then TOK lo rows, 128 B each
+    static constexpr int kScXs = 8 * TOK * 4;                 // the superblock's 8 group sums per row [row][8]
+    static constexpr int kScSlot = kScRows + kScXs + 4 * TOK * 4;  // + scales [row][4]
+    static constexpr int kVBytes = TOK * kTcRows * 4;         // one tile's per-token outputs [token][row]
+    static constexpr int kOffB = kRawStages * kRawStage, kOffSc = kOffB + kBStages * kBBytes,
+                         kOffV = kOffSc + 4 * kScSlot, kSmem = kOffV + kVBytes;
+    // Tensor memory (512 columns): D[db][m] at (db*2+m)*kDCols, A[ab][m] (32
+    // columns = 64 fp16 of one 64-value chunk) at kACol0 + (ab*2+m)*32; small
+    // tiles leave room for a deeper A ring.
+    static constexpr int kDCols = 2 * TOK;
+    static constexpr int kACol0 = 4 * kDCols;
+    static constexpr int kAStages = (512 - kACol0) / 64 >= 4 ? 4 : 2;
+    static_assert(kACol0 + kAStages * 64 <= 512, "tensor memory budget");
+    static_assert(kSmem % 16 == 0 && kScSlot % 16 == 0 && kOffB % 1024 == 0 && kBBytes % 1024 == 0 &&
+                      (TOK * 128) % 1024 == 0, "alignment");
+};
+constexpr int kTokDecode = 32;  // decode: every token tile has at most kMaxDecodeTokens tokens
+static_assert(kTokDecode <= kTcTok, "tile sizes");
 constexpr uint32_t kBad = 1u << 16;
 
 enum { kEnd = 0, kGU = 1, kDN = 2 };
@@ -87,7 +98,7 @@ struct Item {
 struct Bars {
     uint64_t item_full[4], item_empty[4], tab_full[4];
     uint64_t raw_full[kRawStages], raw_empty[kRawStages];
-    uint64_t a_full[2], a_empty[2];
+    uint64_t a_full[4], a_empty[4];
     uint64_t b_full[kBStages], b_empty[kBStages];
     uint64_t d_full[2], d_empty[2];
     uint64_t sc_full[4], sc_empty[4];
@@ -160,6 +171,13 @@ __device__ __forceinline__ uint64_t umma_desc(uint32_t addr, uint32_t lbo, uint3
     return (uint64_t)((addr >> 4) & 0x3FFF) | ((uint64_t)((lbo >> 4) & 0x3FFF) << 16) |
            ((uint64_t)((sbo >> 4) & 0x3FFF) << 32) | ((uint64_t)1 << 46);
 }
+// The same for a K-major tile with 128-byte swizzle (rows of 64 fp16 = 128 B,
+// 8-row atoms 1024 B apart; the tile starts on a 1024-byte boundary). Moving
+// to the next 16-value step adds 32 B (2 units) to the start address.
+__device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t addr) {
+    return (uint64_t)((addr >> 4) & 0x3FFF) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) | ((uint64_t)1 << 46) |
+           ((uint64_t)2 << 61);
+}
 // kind::f16 instruction descriptor: fp32 accumulator, fp16 A and B, both K-major.
 __device__ __forceinline__ uint32_t idesc_f16(int M, int N) {
     return (1u << 4) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
@@ -213,7 +231,7 @@ __device__ __forceinline__ void cp_async4(void *dst, const void *src) {
 }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-__device__ __forceinline__ void cp_async_wait_1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_2() { asm volatile("cp.async.wait_group 2;" ::: "memory"); }
 // Named barrier over n threads that also ANDs a predicate across them.
 __device__ __forceinline__ bool bar_all(int id, int n, bool ok) {
     int r;
@@ -283,23 +301,28 @@ __device__ __forceinline__ float2 mterm2(const float (&mg)[8], const float *xs, 
 }
 
 // Per-item token table, filled by the B stager once per item.
+template <int TOK>
 struct __align__(16) TokTab {
-    int tok[kTcTok];   // token index
-    int src[kTcTok];   // B source row, in halves: x16 row (gate/up) or mid16 row (down)
-    int mrow[kTcTok];  // SwiGLU-output row written (gate/up) or read (down)
-    int slot[kTcTok];  // routed slot t*10+k (down)
-    float w[kTcTok];   // route weight (down)
+    int tok[TOK];   // token index
+    int mrow[TOK];  // SwiGLU-output row written (gate/up) or read (down)
+    int slot[TOK];  // routed slot t*10+k (down)
+    float w[TOK];   // route weight (down)
 };
 
+template <int TOK>
 __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a, const __grid_constant__ TcMaps maps) {
+    using C = Cfg<TOK>;
+    constexpr int kTok = TOK, kBBytes = C::kBBytes, kScXs = C::kScXs, kScSlot = C::kScSlot, kOffB = C::kOffB,
+                  kOffSc = C::kOffSc, kOffV = C::kOffV, kDCols = C::kDCols, kACol0 = C::kACol0,
+                  kAStages = C::kAStages;
     extern __shared__ __align__(1024) unsigned char smem[];
     __shared__ Bars bars;
     __shared__ Item items[4];
-    __shared__ TokTab tabs[4];
-    __shared__ float s_scale[kTcTok];  // power-of-two scale per token of one gate/up tile
+    __shared__ TokTab<TOK> tabs[4];
+    __shared__ float s_scale[kTok];  // power-of-two scale per token of one gate/up tile
     __shared__ uint32_t tmem_base;
     __shared__ volatile int abort_flag;
-    __shared__ int s_combine[kTcTok];
+    __shared__ int s_combine[kTok];
     __shared__ int s_ncombine;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int T = a.T, H = a.H, F = a.F;
@@ -317,9 +340,11 @@ __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a,
             mbar_init(&bars.raw_full[i], 1);
             mbar_init(&bars.raw_empty[i], kConvWarps);
         }
-        for (int i = 0; i < 2; i++) {
+        for (int i = 0; i < kAStages; i++) {
             mbar_init(&bars.a_full[i], kConvWarps);
             mbar_init(&bars.a_empty[i], 2);
+        }
+        for (int i = 0; i < 2; i++) {
             mbar_init(&bars.d_full[i], 2);
             mbar_init(&bars.d_empty[i], kEpiWarps);
             mbar_init(&bars.mma_done[i], 1);
@@ -368,7 +393,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a,
                 }
                 if (it.kind != kEnd) {
                     if (it.sub < a.shared_subs) {  // known without the routing
-                        it.expert = -1, it.tok0 = it.sub * kTcTok, it.n = min(kTcTok, T - it.tok0), it.first = 0;
+                        it.expert = -1, it.tok0 = it.sub * kTok, it.n = min(kTok, T - it.tok0), it.first = 0;
                     } else {
                         it.expert = __ldcg(&a.sub[it.sub].expert);
                         it.first = __ldcg(&a.sub[it.sub].first);
@@ -409,14 +434,13 @@ __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a,
         if (lane == 0) {
             const int mi = warp == kMmaWarp ? 0 : 1;
             int gsb = 0, gch = 0;
-            const uint64_t b_desc0 = umma_desc(smem_u32(smem + kOffB), 128, 1024);
+            const uint64_t b_desc0 = umma_desc_sw128(smem_u32(smem + kOffB));
+            const uint32_t idesc = idesc_f16(kTcRows, 2 * kTok);  // hi and lo rows of every tile row
             for (int seq = 0;; seq++) {
                 const int slot = seq & 3;
                 if (!wait_phase(&bars.item_full[slot], (seq >> 2) & 1, &abort_flag, err)) break;
                 const Item it = items[slot];
                 if (it.kind == kEnd) break;
-                const int n_pad = (it.n + 15) & ~15;
-                const uint32_t idesc = idesc_f16(kTcRows, 2 * n_pad);
                 const bool gu = it.kind == kGU;
                 const int nsb = gu ? gu_sb : dn_sb;
                 bool ok = true;
@@ -426,17 +450,17 @@ __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a,
                     tc_fence_after();
                     const uint32_t d = tmem + (uint32_t)((db * 2 + mi) * kDCols);
                     for (int c = 0; c < 4; c++, gch++) {
-                        const int ab = gch & 1, bs = gch % kBStages;
-                        if (!(ok = wait_phase(&bars.a_full[ab], (gch >> 1) & 1, &abort_flag, err))) break;
+                        const int ab = gch % kAStages, bs = gch % kBStages;
+                        if (!(ok = wait_phase(&bars.a_full[ab], (gch / kAStages) & 1, &abort_flag, err))) break;
                         if (!(ok = wait_phase(&bars.b_full[bs], (gch / kBStages) & 1, &abort_flag, err))) break;
                         if (gu || (c >> 1) == mi) {
                             tc_fence_after();
                             const uint32_t ac = tmem + (uint32_t)(kACol0 + (ab * 2 + (gu ? mi : 0)) * 32);
                             const uint64_t bd = b_desc0 + (uint64_t)((bs * kBBytes) >> 4);
                             mma_ts(d, ac, bd, idesc, gu ? c != 0 : (c & 1) != 0);
-                            mma_ts1(d, ac + 8, bd + 16, idesc);
-                            mma_ts1(d, ac + 16, bd + 32, idesc);
-                            mma_ts1(d, ac + 24, bd + 48, idesc);
+                            mma_ts1(d, ac + 8, bd + 2, idesc);
+                            mma_ts1(d, ac + 16, bd + 4, idesc);
+                            mma_ts1(d, ac + 24, bd + 6, idesc);
                             mma_commit(&bars.a_empty[ab]);
                             mma_commit(&bars.b_empty[bs]);
                         } else {  // the other issuer's chunk: nothing read here
@@ -463,18 +487,15 @@ __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a,
             if (!wait_phase(&bars.item_full[slot], (seq >> 2) & 1, &abort_flag, err)) break;
             const Item it = items[slot];
             if (it.kind == kEnd) break;
-            TokTab &tb = tabs[slot];
+            TokTab<TOK> &tb = tabs[slot];
             const bool gu = it.kind == kGU, sh = it.expert < 0;
-            const int n_pad = (it.n + 15) & ~15, N = 2 * n_pad;
-            const int K = gu ? H : F;
+            const int n_pad = (it.n + 15) & ~15;
+            const int row0 = sh ? T * kTop + it.tok0 : it.first;  // first SwiGLU-output row of the tile
             for (int j = lane; j < n_pad; j += 32) {
-                const int jv = j < it.n ? j : 0;  // padding rows repeat token 0 (their columns are discarded)
+                const int jv = j < it.n ? j : 0;
                 const int sl = sh ? 0 : __ldcg(a.pairs + it.first + jv);
-                const int tok = sh ? it.tok0 + jv : sl / kTop;
-                const int mrow = sh ? T * kTop + it.tok0 + jv : it.first + jv;
-                tb.tok[j] = tok;
-                tb.mrow[j] = mrow;
-                tb.src[j] = gu ? tok * 2 * H : mrow * 2 * F;
+                tb.tok[j] = sh ? it.tok0 + jv : sl / kTop;
+                tb.mrow[j] = row0 + jv;
                 tb.slot[j] = sl;
                 tb.w[j] = (sh || gu) ? 0.0f : __ldcg(a.wts + sl);
             }
@@ -485,74 +506,39 @@ __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a,
                 ok = !abort_flag;
             }
             __syncwarp();
-            if (lane == 0) arrive(&bars.tab_full[slot]);
-            const __half *bsrc = gu ? a.x16 : a.mid16;
-            const float *gsums = gu ? a.xsum : a.msum;
-            const int ngroups = K / 32;
-            const int nsb = gu ? gu_sb : dn_sb;
-            for (int sb = 0; sb < nsb && ok; sb++, gsb++) {
-                const int sc_slot = gsb & 3;
-                if (gsb >= 4 && !(ok = wait_phase(&bars.sc_empty[sc_slot], ((gsb >> 2) - 1) & 1, &abort_flag, err)))
-                    break;
-                // group sums and 1/s of this superblock's tokens (zero for padding), copied
-                // with the first chunk's B rows
-                unsigned char *scb = smem + kOffSc + sc_slot * kScSlot;
-                float *xs = reinterpret_cast<float *>(scb + kScRows);
-                float *inv2 = reinterpret_cast<float *>(scb + kScRows + kScXs);
-                for (int j = lane; j < n_pad; j += 32) {
-                    if (j < it.n) {
-                        const int grow = gu ? tb.tok[j] : tb.mrow[j];
-                        const float *gp = gsums + (size_t)grow * ngroups + sb * 8;
-                        cp_async16(xs + j * 8, gp);
-                        cp_async16(xs + j * 8 + 4, gp + 4);
-                        const float *ip = gu ? a.xinv + grow : a.midinv + (size_t)grow * gu_mt + 2 * sb;
-                        cp_async4(inv2 + j, ip);
-                        cp_async4(inv2 + kTcTok + j, gu ? ip : ip + 1);
-                    } else {
-                        reinterpret_cast<float4 *>(xs + j * 8)[0] = make_float4(0.f, 0.f, 0.f, 0.f);
-                        reinterpret_cast<float4 *>(xs + j * 8)[1] = make_float4(0.f, 0.f, 0.f, 0.f);
-                        inv2[j] = 0.0f;
-                        inv2[kTcTok + j] = 0.0f;
-                    }
-                }
-                // B rows of the four 64-value chunks: token j hi -> row j, lo -> row n_pad + j.
-                // Eight consecutive lanes fill the eight rows of one core matrix (128 B).
-                for (int c = 0; c < 4; c++, gch++) {
-                    const int bs = gch % kBStages;
-                    if (gch >= kBStages &&
-                        !(ok = wait_phase(&bars.b_empty[bs], (gch / kBStages - 1) & 1, &abort_flag, err)))
+            if (lane == 0) {
+                arrive(&bars.tab_full[slot]);
+                // B tile rows: all T tokens (per-token activations) or the tile's own rows
+                const int brow = (gu && a.all_tok) ? 0 : row0;
+                const CUtensorMap *bh = gu ? &maps.bx_hi : &maps.bm_hi, *bl = gu ? &maps.bx_lo : &maps.bm_lo;
+                const CUtensorMap *gs = gu ? &maps.sx : &maps.sm, *iv = gu ? &maps.ix : &maps.im;
+                const int nsb = gu ? gu_sb : dn_sb;
+                for (int sb = 0; sb < nsb && ok; sb++, gsb++) {
+                    const int sc_slot = gsb & 3;
+                    if (gsb >= 4 && !(ok = wait_phase(&bars.sc_empty[sc_slot], ((gsb >> 2) - 1) & 1, &abort_flag, err)))
                         break;
-                    const int u = sb * 4 + c;
-                    unsigned char *bt = smem + kOffB + bs * kBBytes;
-                    for (int sgi = lane; sgi < N * 8; sgi += 32) {
-                        const int rr = sgi & 7, kb = (sgi >> 3) & 7, row = (sgi >> 6) * 8 + rr;
-                        const int j = row < n_pad ? row : row - n_pad, hl = row < n_pad ? 0 : 1;
-                        cp_async16(bt + ((row >> 3) * 8 + kb) * 128 + rr * 16,
-                                   bsrc + (size_t)tb.src[j] + hl * K + u * 64 + kb * 8);
-                    }
-                    cp_async_commit();
-                    if (c > 0) {  // the previous chunk (and with chunk 0 the group sums) has landed
-                        cp_async_wait_1();
-                        fence_proxy_async();
-                        __syncwarp();
-                        if (lane == 0) {
-                            arrive(&bars.b_full[(gch - 1) % kBStages]);
-                            if (c == 1) arrive(&bars.sc_full[sc_slot]);
-                        }
+                    unsigned char *scb = smem + kOffSc + sc_slot * kScSlot;
+                    mbar_arrive_expect_tx(&bars.sc_full[sc_slot], kScXs + 4 * kTok * 4);
+                    tma_2d(scb + kScRows, gs, sb * 8, brow, &bars.sc_full[sc_slot]);
+                    tma_2d(scb + kScRows + kScXs, iv, gu ? 0 : (2 * sb) & ~3, brow, &bars.sc_full[sc_slot]);
+                    for (int c = 0; c < 4; c++, gch++) {
+                        const int bs = gch % kBStages;
+                        if (gch >= kBStages &&
+                            !(ok = wait_phase(&bars.b_empty[bs], (gch / kBStages - 1) & 1, &abort_flag, err)))
+                            break;
+                        unsigned char *bt = smem + kOffB + bs * kBBytes;
+                        mbar_arrive_expect_tx(&bars.b_full[bs], kBBytes);
+                        tma_2d(bt, bh, (sb * 4 + c) * 64, brow, &bars.b_full[bs]);
+                        tma_2d(bt + kTok * 128, bl, (sb * 4 + c) * 64, brow, &bars.b_full[bs]);
                     }
                 }
-                if (!ok) break;
-                cp_async_wait_all();
-                fence_proxy_async();
-                __syncwarp();
-                if (lane == 0) arrive(&bars.b_full[(gch - 1) % kBStages]);
+                arrive(&bars.item_empty[slot]);
             }
-            cp_async_wait_all();
-            __syncwarp();
-            if (lane == 0) arrive(&bars.item_empty[slot]);
+            ok = __shfl_sync(0xffffffffu, ok, 0);
             if (!ok) break;
         }
-        cp_async_wait_all();
+        if (lane == 0)  // copies still in flight land before the CTA may exit
+            for (int k = max(0, gch - kBStages); k < gch; k++) wait_drain(&bars.b_full[k % kBStages], (k / kBStages) & 1);
     } else if (warp >= kConvWarp0 && warp < kEpiWarp0) {
         // ------------------------------------------------------ converters
         regs_dec();
@@ -581,8 +567,9 @@ __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a,
                     if (lane == 0) arrive(&bars.sc_full[sc_slot]);
                 }
                 for (int c = 0; c < 4; c++, gch++) {
-                    const int ab = gch & 1;
-                    if (gch >= 2 && !(ok = wait_phase(&bars.a_empty[ab], ((gch >> 1) - 1) & 1, &abort_flag, err)))
+                    const int ab = gch % kAStages;
+                    if (gch >= kAStages &&
+                        !(ok = wait_phase(&bars.a_empty[ab], (gch / kAStages - 1) & 1, &abort_flag, err)))
                         break;
                     tc_fence_after();
                     for (int m = 0; m < mats; m++) {
@@ -611,17 +598,21 @@ __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a,
         const int r = 32 * q + lane;             // row within the tile
         const int half = ew >> 2;                // token half
         const int et = tid - kEpiWarp0 * 32;     // 0..255
-        constexpr int kHalf = kTcTok / 2;        // tokens per half, at most
+        constexpr int kHalf = kTok / 2;        // tokens per half, at most
         int gsb = 0;
         for (int seq = 0;; seq++) {
             const int slot = seq & 3;
             bool ok = wait_phase(&bars.item_full[slot], (seq >> 2) & 1, &abort_flag, err);
             const Item it = items[slot];
             if (!bar_all(3, 256, ok) || it.kind == kEnd) break;
-            const TokTab &tb = tabs[slot];
-            const int n_pad = (it.n + 15) & ~15, hw = n_pad >> 1;  // tokens per half (multiple of 8)
-            const int j0 = half * hw;
+            const TokTab<TOK> &tb = tabs[slot];
             const bool gu = it.kind == kGU;
+            // D columns c (hi) and kTok + c (lo): token c of all T tokens (gate/up on
+            // per-token activations) or row c of the tile
+            const bool by_tok = gu && a.all_tok;
+            const int ncol = by_tok ? ((T + 15) & ~15) : ((it.n + 15) & ~15);
+            const int hw = ncol >> 1;  // columns per half (multiple of 8)
+            const int j0 = half * hw;
             const int nsb = gu ? gu_sb : dn_sb;
             float2 acc[2][kHalf / 2];
 #pragma unroll
@@ -636,7 +627,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a,
                 const unsigned char *scb = smem + kOffSc + sc_slot * kScSlot;
                 const uint4 *scs = reinterpret_cast<const uint4 *>(scb);
                 const float *xs = reinterpret_cast<const float *>(scb + kScRows);
-                const float *inv2 = reinterpret_cast<const float *>(scb + kScRows + kScXs);
+                const float *inv4 = reinterpret_cast<const float *>(scb + kScRows + kScXs);  // [row][4]
                 const uint32_t lanes = tmem + ((uint32_t)(32 * q) << 16);
                 const float2 k2048 = make_float2(1.0f / 2048.0f, 1.0f / 2048.0f);
                 if (gu) {
@@ -654,14 +645,14 @@ __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a,
                             if (cb * 8 >= hw) break;
                             uint32_t rh[8], rl[8];
                             tmem_ld8_nw(col0 + j0 + cb * 8, rh);
-                            tmem_ld8_nw(col0 + n_pad + j0 + cb * 8, rl);
+                            tmem_ld8_nw(col0 + kTok + j0 + cb * 8, rl);
                             tmem_wait_ld();
 #pragma unroll
                             for (int pp = 0; pp < 4; pp++) {
                                 const int j = j0 + cb * 8 + 2 * pp;
                                 const float2 hi = make_float2(__uint_as_float(rh[2 * pp]), __uint_as_float(rh[2 * pp + 1]));
                                 const float2 lo = make_float2(__uint_as_float(rl[2 * pp]), __uint_as_float(rl[2 * pp + 1]));
-                                const float2 inv = *reinterpret_cast<const float2 *>(&inv2[j]);
+                                const float2 inv = make_float2(inv4[j * 4], inv4[j * 4 + 4]);
                                 const float2 dot = __fmul2_rn(__ffma2_rn(lo, k2048, hi), inv);
                                 const float2 mt = mterm2(mg, xs, j);
                                 float2 &ac = acc[m][cb * 4 + pp];
@@ -678,6 +669,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a,
 #pragma unroll
                     for (int g = 0; g < 8; g++) mg[g] = (float)(((g < 4 ? sv.z : sv.w) >> (8 * (g & 3))) & 0xFFu);
                     const uint32_t c0 = lanes + (uint32_t)((db * 2) * kDCols);
+                    const int ioff = (2 * sb) & 3;  // this superblock's two scales within the loaded four
 #pragma unroll
                     for (int cb = 0; cb < kHalf / 8; cb++) {
                         if (cb * 8 >= hw) break;
@@ -685,14 +677,14 @@ __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a,
                         for (int h = 0; h < 2; h++) {  // the two 128-value halves, one B scale each
                             uint32_t rh[8], rl[8];
                             tmem_ld8_nw(c0 + h * kDCols + j0 + cb * 8, rh);
-                            tmem_ld8_nw(c0 + h * kDCols + n_pad + j0 + cb * 8, rl);
+                            tmem_ld8_nw(c0 + h * kDCols + kTok + j0 + cb * 8, rl);
                             tmem_wait_ld();
 #pragma unroll
                             for (int pp = 0; pp < 4; pp++) {
                                 const int j = j0 + cb * 8 + 2 * pp;
                                 const float2 v = __ffma2_rn(make_float2(__uint_as_float(rl[2 * pp]), __uint_as_float(rl[2 * pp + 1])), k2048,
                                                             make_float2(__uint_as_float(rh[2 * pp]), __uint_as_float(rh[2 * pp + 1])));
-                                const float2 dot = __fmul2_rn(v, *reinterpret_cast<const float2 *>(&inv2[h * kTcTok + j]));
+                                const float2 dot = __fmul2_rn(v, make_float2(inv4[j * 4 + ioff + h], inv4[j * 4 + 4 + ioff + h]));
                                 float2 &ac = acc[0][cb * 4 + pp];
                                 ac = __ffma2_rn(d2, dot, ac);
                                 if (h) ac = __ffma2_rn(nm2, mterm2(mg, xs, j), ac);
@@ -735,7 +727,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a,
                 // scale from the tile's max |v|
 #pragma unroll 1
                 for (int j = ew; j < it.n; j += kEpiWarps) {
-                    const float *vj = sv + j * kTcRows;
+                    const float *vj = sv + (by_tok ? tb.tok[j] : j) * kTcRows;
                     const float v0 = vj[lane], v1 = vj[32 + lane], v2 = vj[64 + lane], v3 = vj[96 + lane];
                     float s0 = v0, s1 = v1, s2 = v2, s3 = v3;
 #pragma unroll
@@ -752,7 +744,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a,
                         pow2_scale(__uint_as_float(mb), sc, inv);
                         const size_t mrow = (size_t)tb.mrow[j];
                         *reinterpret_cast<float4 *>(a.msum + mrow * (F / 32) + it.mt * 4) = make_float4(s0, s1, s2, s3);
-                        a.midinv[mrow * gu_mt + it.mt] = inv;
+                        a.midinv[mrow * a.mi_stride + it.mt] = inv;
                         s_scale[j] = sc;
                     }
                 }
@@ -760,7 +752,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a,
                 // fp16 hi/lo split of v*s for the down tiles
 #pragma unroll 1
                 for (int j = et >> 7; j < it.n; j += 2) {
-                    const float v = sv[j * kTcRows + rr] * s_scale[j];
+                    const float v = sv[(by_tok ? tb.tok[j] : j) * kTcRows + rr] * s_scale[j];
                     const __half hi = __float2half_rn(v);
                     const size_t base = (size_t)tb.mrow[j] * 2 * F + it.mt * kTcRows + rr;
                     a.mid16[base] = hi;
@@ -831,7 +823,23 @@ __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a,
 
 __global__ void tc_prep_kernel(const float *x, int H, __half *x16, float *xinv, float *xsum) {
     const int t = blockIdx.x;
-    tc_prep_token(x + (size_t)t * H, H, x16 + (size_t)t * 2 * H, xinv + t, xsum + (size_t)t * (H / 32));
+    tc_prep_token(x + (size_t)t * H, H, x16 + (size_t)t * 2 * H, xinv + (size_t)t * 4, xsum + (size_t)t * (H / 32));
+}
+
+// One routed row per CTA: rows [0, n_pairs) are the plan's (token, expert)
+// pairs in expert order, rows T*10 + t the shared expert's tokens.
+__global__ void tc_prep_rows_kernel(const float *x, int T, int H, const int *pairs, const int *n_pairs, __half *x16,
+                                    float *xinv, float *xsum) {
+    const int row = blockIdx.x;
+    int tok;
+    if (row < T * kTop) {
+        if (row >= __ldcg(n_pairs)) return;
+        tok = __ldcg(pairs + row) / kTop;
+    } else {
+        tok = row - T * kTop;
+    }
+    tc_prep_token(x + (size_t)tok * H, H, x16 + (size_t)row * 2 * H, xinv + (size_t)row * 4,
+                  xsum + (size_t)row * (H / 32));
 }
 
 using EncodeTiled = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
@@ -850,20 +858,27 @@ EncodeTiled encoder() {
     return fn;
 }
 
-// 2-D byte tensor [rows][row_bytes] read in boxes of one Q4_K superblock
-// (144 bytes) by 128 rows.
-int make_map(CUtensorMap *m, const void *base, size_t rows, size_t row_bytes) {
+// 2-D tensor [rows][inner] (row pitch in bytes) read in boxes of box_inner x box_rows.
+int make_map_2d(CUtensorMap *m, CUtensorMapDataType dt, int esize, const void *base, size_t inner, size_t rows,
+                size_t pitch, uint32_t box_inner, uint32_t box_rows, CUtensorMapSwizzle sw) {
     EncodeTiled fn = encoder();
     if (!fn) return cudaErrorNotSupported;
-    if (!base || (reinterpret_cast<uintptr_t>(base) & 15) || row_bytes % 16) return cudaErrorInvalidValue;
-    cuuint64_t dims[2] = {row_bytes, rows};
-    cuuint64_t strides[1] = {row_bytes};
-    cuuint32_t box[2] = {144, (cuuint32_t)kTcRows};
+    if (!base || (reinterpret_cast<uintptr_t>(base) & 15) || pitch % 16 || (box_inner * esize) % 16 || rows == 0)
+        return cudaErrorInvalidValue;
+    cuuint64_t dims[2] = {inner, rows};
+    cuuint64_t strides[1] = {pitch};
+    cuuint32_t box[2] = {box_inner, box_rows};
     cuuint32_t estr[2] = {1, 1};
-    CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(base), dims, strides, box, estr,
-                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    CUresult r = fn(m, dt, 2, const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS ? 0 : cudaErrorInvalidValue;
+}
+
+// Q4_K rows [rows][row_bytes] read one superblock (144 bytes) x 128 rows at a time.
+int make_map(CUtensorMap *m, const void *base, size_t rows, size_t row_bytes) {
+    if (row_bytes % 16) return cudaErrorInvalidValue;
+    return make_map_2d(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, base, row_bytes, rows, row_bytes, 144, kTcRows,
+                       CU_TENSOR_MAP_SWIZZLE_NONE);
 }
 
 int sm_count_tc() {
@@ -884,10 +899,14 @@ bool tc_supported(int H, int F, int QG, int QD) {
     return QG == 12 && QD == 12 && H % 256 == 0 && F % 256 == 0 && H >= 256 && F >= 256 && encoder() != nullptr;
 }
 
-size_t tc_smem_bytes() { return kSmem; }
+size_t tc_smem_bytes() { return Cfg<kTcTok>::kSmem; }
 
-int tc_make_maps(const TcArgs &a, TcMaps &m) {
-    const size_t E = kExperts;
+int tc_make_maps(const TcArgs &a, TcMaps &m, int tok) {
+    const size_t E = kExperts, H = a.H, F = a.F;
+    const size_t rows = (size_t)a.T * kTop + a.T;        // routed pairs + shared tokens
+    const size_t xrows = a.all_tok ? (size_t)a.T : rows;  // rows of the gate/up activations
+    const auto f16 = CU_TENSOR_MAP_DATA_TYPE_FLOAT16, f32 = CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+    const auto sw = CU_TENSOR_MAP_SWIZZLE_128B, none = CU_TENSOR_MAP_SWIZZLE_NONE;
     int rc = make_map(&m.gate, a.gate, E * a.F, a.grb);
     if (!rc) rc = make_map(&m.up, a.up, E * a.F, a.grb);
     if (!rc) rc = make_map(&m.down, a.down, E * a.H, a.drb);
@@ -899,27 +918,51 @@ int tc_make_maps(const TcArgs &a, TcMaps &m) {
         m.su = m.up;
         m.sd = m.down;
     }
+    // activations and SwiGLU outputs: [row][2][K] fp16, hi plane then lo plane
+    if (!rc) rc = make_map_2d(&m.bx_hi, f16, 2, a.x16, H, xrows, 4 * H, 64, tok, sw);
+    if (!rc) rc = make_map_2d(&m.bx_lo, f16, 2, a.x16 + H, H, xrows, 4 * H, 64, tok, sw);
+    if (!rc) rc = make_map_2d(&m.bm_hi, f16, 2, a.mid16, F, rows, 4 * F, 64, tok, sw);
+    if (!rc) rc = make_map_2d(&m.bm_lo, f16, 2, a.mid16 + F, F, rows, 4 * F, 64, tok, sw);
+    if (!rc) rc = make_map_2d(&m.sx, f32, 4, a.xsum, H / 32, xrows, H / 8, 8, tok, none);
+    if (!rc) rc = make_map_2d(&m.sm, f32, 4, a.msum, F / 32, rows, F / 8, 8, tok, none);
+    if (!rc) rc = make_map_2d(&m.ix, f32, 4, a.xinv, 4, xrows, 16, 4, tok, none);
+    if (!rc) rc = make_map_2d(&m.im, f32, 4, a.midinv, a.mi_stride, rows, 4 * (size_t)a.mi_stride, 4, tok, none);
     return rc;
 }
 
-int tc_launch(const TcArgs &a, const TcMaps &m, cudaStream_t st, bool pdl) {
-    int rc = cudaFuncSetAttribute(tc_experts_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+template <int TOK>
+int tc_launch_tok(const TcArgs &a, const TcMaps &m, cudaStream_t st, bool pdl) {
+    constexpr int smem = Cfg<TOK>::kSmem;
+    int rc = cudaFuncSetAttribute(tc_experts_kernel<TOK>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (rc) return rc;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(sm_count_tc());
     cfg.blockDim = dim3(kThreads);
-    cfg.dynamicSmemBytes = kSmem;
+    cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, tc_experts_kernel, a, m);
+    return cudaLaunchKernelEx(&cfg, tc_experts_kernel<TOK>, a, m);
+}
+
+int tc_launch(const TcArgs &a, const TcMaps &m, cudaStream_t st, bool pdl, int max_tile) {
+    if (max_tile <= kTokDecode) return tc_launch_tok<kTokDecode>(a, m, st, pdl);
+    if (max_tile <= kTcTok) return tc_launch_tok<kTcTok>(a, m, st, pdl);
+    return cudaErrorInvalidValue;
 }
 
 int tc_prep_launch(const float *x, int T, int H, __half *x16, float *xinv, float *xsum, cudaStream_t st) {
     tc_prep_kernel<<<T, 256, 0, st>>>(x, H, x16, xinv, xsum);
+    return cudaGetLastError();
+}
+
+int tc_prep_rows_launch(const float *x, int T, int H, const int *pairs, const int *n_pairs, bool shared, __half *x16,
+                        float *xinv, float *xsum, cudaStream_t st) {
+    const int rows = T * kTop + (shared ? T : 0);
+    tc_prep_rows_kernel<<<rows, 256, 0, st>>>(x, T, H, pairs, n_pairs, x16, xinv, xsum);
     return cudaGetLastError();
 }
 

@@ -18,9 +18,13 @@ struct TcArgs {
     int T, H, F;
     const unsigned char *gate, *up, *down, *sg, *su, *sd;  // Q4_K experts (+ shared), gate/up rows hold H values
     size_t grb, drb;
-    const __half *x16;     // [T][2][H]: x*s hi, (x*s - hi)*2048 lo, s a power of two per token
-    const float *xinv;     // [T]: 1/s
-    const float *xsum;     // [T][H/32]: 32-value group sums of x
+    // Gate/up activations: either per token (all_tok = 1: every gate/up tile
+    // multiplies all T <= tile tokens and keeps its own columns) or per routed
+    // row (rows as for the SwiGLU outputs below, filled by tc_prep_rows_launch).
+    int all_tok;
+    const __half *x16;     // [T or rows][2][H]: x*s hi, (x*s - hi)*2048 lo, s a power of two per row
+    const float *xinv;     // [T or rows][4]: 1/s in element 0
+    const float *xsum;     // [T or rows][H/32]: 32-value group sums of x
     const SubJob *sub;     // shared sub-jobs first, then routed
     const int *n_sub;      // device count of sub-jobs
     int shared_subs;       // number of shared sub-jobs (known before routing)
@@ -31,7 +35,8 @@ struct TcArgs {
     const float *sgate;    // [T] shared-gate logits, or null
     // SwiGLU outputs, one row per routed pair p (row p) and shared token t (row T*10+t):
     __half *mid16;         // [rows][2][F]: v*s hi, (v*s - hi)*2048 lo, s per 128-value tile
-    float *midinv;         // [rows][F/128]: 1/s
+    float *midinv;         // [rows][mi_stride]: 1/s per 128-value tile
+    int mi_stride;         // F/128 rounded up to a multiple of 4
     float *msum;           // [rows][F/32]: 32-value group sums of v
     float *slots;          // [T*10][H]
     float *shout;          // [T][H]
@@ -44,15 +49,23 @@ struct TcArgs {
 };
 
 struct TcMaps {
-    CUtensorMap gate, up, down, sg, su, sd;
+    CUtensorMap gate, up, down, sg, su, sd;  // raw Q4_K rows, one superblock x 128 rows per box
+    CUtensorMap bx_hi, bx_lo, bm_hi, bm_lo;  // B rows (activations, SwiGLU outputs), 64 values x tile rows, 128B swizzle
+    CUtensorMap sx, sm, ix, im;              // their group sums (8 x tile rows) and scales (4 x tile rows)
 };
 
 bool tc_supported(int H, int F, int QG, int QD);
 size_t tc_smem_bytes();
-int tc_make_maps(const TcArgs &a, TcMaps &m);
-int tc_launch(const TcArgs &a, const TcMaps &m, cudaStream_t st, bool pdl);
+int tc_make_maps(const TcArgs &a, TcMaps &m, int max_tile);
+// max_tile: the largest token tile of the launch (sub-jobs, and the split of
+// the shared expert's tokens: shared sub-job i covers tokens i*max_tile ..).
+int tc_launch(const TcArgs &a, const TcMaps &m, cudaStream_t st, bool pdl, int max_tile);
 // x16 / xinv / xsum for T tokens (one CTA per token)
 int tc_prep_launch(const float *x, int T, int H, __half *x16, float *xinv, float *xsum, cudaStream_t st);
+// The same per routed row: rows [0, *n_pairs) take token pairs[row]/10, rows
+// T*10 + t (when shared) token t.
+int tc_prep_rows_launch(const float *x, int T, int H, const int *pairs, const int *n_pairs, bool shared, __half *x16,
+                        float *xinv, float *xsum, cudaStream_t st);
 
 // Power of two s with max|v*s| in [2^13, 2^14) for mx = max|v| (s = 1 when
 // mx is zero, subnormal-small or not finite), and 1/s, both built from the
