@@ -127,25 +127,42 @@ __global__ void __launch_bounds__(128) dec_router_kernel(DecArgs a) {
         ok = mbar_wait_bounded(&bar, 0, &a.hdr->error);
     }
     if (!__syncthreads_or(!ok)) {
-        if (warp < nrows) {
-            float acc[TMAX];
+        if (nrows > 0) {
+            // warp w: tokens w, w+4, ... against every staged row; lane j sums
+            // k = j, j+32, ... in order (the reference's 32-lane order)
+            constexpr int kTpw = (TMAX + 3) / 4;
+            float acc[kRouterRows][kTpw];
 #pragma unroll
-            for (int t = 0; t < TMAX; t++) acc[t] = 0.0f;
-            const float *w = wr + (size_t)warp * H;
+            for (int r = 0; r < kRouterRows; r++)
+#pragma unroll
+                for (int i = 0; i < kTpw; i++) acc[r][i] = 0.0f;
             for (int k = lane; k < H; k += 32) {
-                const float wv = w[k];
+                float wv[kRouterRows];
 #pragma unroll
-                for (int t = 0; t < TMAX; t++)
-                    if (t < T) acc[t] = __fmaf_rn(wv, xs[(size_t)t * H + k], acc[t]);
+                for (int r = 0; r < kRouterRows; r++) wv[r] = r < nrows ? wr[(size_t)r * H + k] : 0.0f;
+#pragma unroll
+                for (int i = 0; i < kTpw; i++) {
+                    const int t = warp + 4 * i;
+                    if (t < T) {
+                        const float xv = xs[(size_t)t * H + k];
+#pragma unroll
+                        for (int r = 0; r < kRouterRows; r++) acc[r][i] = __fmaf_rn(wv[r], xv, acc[r][i]);
+                    }
+                }
             }
-            const int row = row0 + warp;
 #pragma unroll
-            for (int t = 0; t < TMAX; t++) {
-                if (t < T) {
-                    const float s = lane_tree(acc[t]);
-                    if (lane == 0) {
-                        if (row < kExperts) a.logits[t * kExperts + row] = s;
-                        else a.sgate[t] = s;
+            for (int r = 0; r < kRouterRows; r++) {
+                if (r >= nrows) break;
+                const int row = row0 + r;
+#pragma unroll
+                for (int i = 0; i < kTpw; i++) {
+                    const int t = warp + 4 * i;
+                    if (t < T) {
+                        const float s = lane_tree(acc[r][i]);
+                        if (lane == 0) {
+                            if (row < kExperts) a.logits[t * kExperts + row] = s;
+                            else a.sgate[t] = s;
+                        }
                     }
                 }
             }

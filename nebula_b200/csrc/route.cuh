@@ -3,6 +3,15 @@
 #include "common.cuh"
 
 namespace nb {
+// Order-preserving map of finite floats to unsigned keys (and back).
+__device__ __forceinline__ uint32_t float_key(float v) {
+    const uint32_t u = __float_as_uint(v);
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+__device__ __forceinline__ float key_float(uint32_t k) {
+    return __uint_as_float((k & 0x80000000u) ? (k & 0x7FFFFFFFu) : ~k);
+}
+
 // Top-10 of 512 for one token, run by a full warp. Reference semantics
 // (qwen/gpu.cu:456-465): any non-finite logit -> ids -1, weights 0; ten
 // argmax passes with lowest-index tie break; w = expf(s - max), divided by
@@ -26,37 +35,36 @@ __device__ __forceinline__ void route_token_warp(const float *logits, const floa
         }
         return;
     }
+    // Each lane keeps the best of its 16 values as an order-preserving key; a
+    // pick is two warp reductions: the largest key, then the lowest index among
+    // the lanes holding it. Only the winning lane rescans its values.
+    uint32_t key[16];
+#pragma unroll
+    for (int m = 0; m < 16; m++) key[m] = float_key(v[m] + 0.0f);  // -0 ties with +0, as in the comparison
+    uint32_t bk = key[0];
+    int bm = 0;
+#pragma unroll
+    for (int m = 1; m < 16; m++)
+        if (key[m] > bk) bk = key[m], bm = m;
     float sel_w[kTop];
     int sel_id[kTop];
     float largest = 0.0f;
 #pragma unroll
     for (int k = 0; k < kTop; k++) {
-        // lane-local best: highest value, then lowest index (indices grow with m)
-        float bv = v[0];
-        int bm = 0;
-#pragma unroll
-        for (int m = 1; m < 16; m++)
-            if (v[m] > bv) {
-                bv = v[m];
-                bm = m;
-            }
-        int bi = bm * 32 + lane;
-#pragma unroll
-        for (int d = 16; d; d >>= 1) {
-            float ov = __shfl_xor_sync(0xffffffffu, bv, d);
-            int oi = __shfl_xor_sync(0xffffffffu, bi, d);
-            if (ov > bv || (ov == bv && oi < bi)) {
-                bv = ov;
-                bi = oi;
-            }
-        }
+        const uint32_t mk = __reduce_max_sync(0xffffffffu, bk);
+        const int bi = (int)__reduce_min_sync(0xffffffffu, bk == mk ? (uint32_t)(bm * 32 + lane) : 0xFFFFu);
+        const float bv = key_float(mk);
         if (k == 0) largest = bv;  // the first pick is the maximum of all 512
         sel_id[k] = bi;
         sel_w[k] = expf(bv - largest);
         if ((bi & 31) == lane) {
 #pragma unroll
             for (int m = 0; m < 16; m++)
-                if (m == (bi >> 5)) v[m] = -INFINITY;
+                if (m == (bi >> 5)) key[m] = 0;  // below every finite value
+            bk = key[0], bm = 0;
+#pragma unroll
+            for (int m = 1; m < 16; m++)
+                if (key[m] > bk) bk = key[m], bm = m;
         }
     }
     if (lane == 0) {
