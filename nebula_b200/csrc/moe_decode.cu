@@ -44,6 +44,7 @@ using namespace nb;
 namespace {
 
 constexpr int kRouterRows = 4;   // router rows per K1 CTA
+constexpr int kK1Threads = 512;  // one expert per thread in the plan
 constexpr int kGuRows = 32;      // gate rows (and up rows) per gate/up tile
 constexpr int kConsumers = 8;    // warps in K2; thread 0 also produces
 constexpr int kK2Threads = kConsumers * 32;
@@ -88,7 +89,7 @@ __device__ bool wait_geq(const int *p, int target, int *err) {
 
 // ------------------------------------------------------------------ K1
 template <int QG, int TMAX>
-__global__ void __launch_bounds__(128) dec_router_kernel(DecArgs a) {
+__global__ void __launch_bounds__(kK1Threads) dec_router_kernel(DecArgs a) {
     extern __shared__ __align__(128) unsigned char smem[];
     __shared__ uint64_t bar;
     __shared__ int s_last;
@@ -128,37 +129,30 @@ __global__ void __launch_bounds__(128) dec_router_kernel(DecArgs a) {
     }
     if (!__syncthreads_or(!ok)) {
         if (nrows > 0) {
-            // warp w: tokens w, w+4, ... against every staged row; lane j sums
+            // warp w: staged row w%4 against tokens w/4, w/4+4, ...; lane j sums
             // k = j, j+32, ... in order (the reference's 32-lane order)
-            constexpr int kTpw = (TMAX + 3) / 4;
-            float acc[kRouterRows][kTpw];
+            constexpr int kTg = kK1Threads / 32 / kRouterRows;  // token groups
+            constexpr int kTpw = (TMAX + kTg - 1) / kTg;
+            const int r = warp % kRouterRows, tg = warp / kRouterRows;
+            if (r < nrows) {
+                float acc[kTpw];
 #pragma unroll
-            for (int r = 0; r < kRouterRows; r++)
+                for (int i = 0; i < kTpw; i++) acc[i] = 0.0f;
+                const float *w = wr + (size_t)r * H;
+                for (int k = lane; k < H; k += 32) {
+                    const float wv = w[k];
 #pragma unroll
-                for (int i = 0; i < kTpw; i++) acc[r][i] = 0.0f;
-            for (int k = lane; k < H; k += 32) {
-                float wv[kRouterRows];
-#pragma unroll
-                for (int r = 0; r < kRouterRows; r++) wv[r] = r < nrows ? wr[(size_t)r * H + k] : 0.0f;
-#pragma unroll
-                for (int i = 0; i < kTpw; i++) {
-                    const int t = warp + 4 * i;
-                    if (t < T) {
-                        const float xv = xs[(size_t)t * H + k];
-#pragma unroll
-                        for (int r = 0; r < kRouterRows; r++) acc[r][i] = __fmaf_rn(wv[r], xv, acc[r][i]);
+                    for (int i = 0; i < kTpw; i++) {
+                        const int t = tg + kTg * i;
+                        if (t < T) acc[i] = __fmaf_rn(wv, xs[(size_t)t * H + k], acc[i]);
                     }
                 }
-            }
-#pragma unroll
-            for (int r = 0; r < kRouterRows; r++) {
-                if (r >= nrows) break;
                 const int row = row0 + r;
 #pragma unroll
                 for (int i = 0; i < kTpw; i++) {
-                    const int t = warp + 4 * i;
+                    const int t = tg + kTg * i;
                     if (t < T) {
-                        const float s = lane_tree(acc[r][i]);
+                        const float s = lane_tree(acc[i]);
                         if (lane == 0) {
                             if (row < kExperts) a.logits[t * kExperts + row] = s;
                             else a.sgate[t] = s;
@@ -197,7 +191,7 @@ __global__ void __launch_bounds__(128) dec_router_kernel(DecArgs a) {
     __shared__ unsigned s_bm[kExperts];
     __shared__ int s_off[kExperts];
     __shared__ int s_bad[kMaxDecodeTokens];
-    __shared__ int s_wt[4], s_wu[4], s_inv[4];
+    __shared__ int s_wt[kK1Threads / 32], s_wu[kK1Threads / 32], s_inv[kK1Threads / 32];
     if (a.router) {
         for (int t = warp; t < T; t += blockDim.x / 32)
             route_token_warp(a.logits + t * kExperts, a.bias, a.ids + t * kTop, a.wts + t * kTop);
@@ -230,16 +224,11 @@ __global__ void __launch_bounds__(128) dec_router_kernel(DecArgs a) {
     }
     __syncthreads();
     {
-        // 4 experts per thread: counts, exclusive offsets, ascending used list
-        const int e0 = tid * 4;
-        int c4[4], tot = 0, used = 0;
-#pragma unroll
-        for (int j = 0; j < 4; j++) {
-            c4[j] = __popc(s_bm[e0 + j]);
-            tot += c4[j];
-            used += c4[j] > 0;
-        }
-        int st = tot, su = used;
+        // one expert per thread: counts, exclusive offsets, ascending used list
+        static_assert(kK1Threads == kExperts, "one expert per thread");
+        const int e = tid;
+        const int c = __popc(s_bm[e]), used = c > 0;
+        int st = c, su = used;
 #pragma unroll
         for (int d = 1; d < 32; d <<= 1) {
             const int vt = __shfl_up_sync(0xffffffffu, st, d), vu = __shfl_up_sync(0xffffffffu, su, d);
@@ -258,23 +247,18 @@ __global__ void __launch_bounds__(128) dec_router_kernel(DecArgs a) {
             bt += s_wt[w];
             bu += s_wu[w];
         }
-        int ot = bt + st - tot, ou = bu + su - used;
-#pragma unroll
-        for (int j = 0; j < 4; j++) {
-            const int e = e0 + j;
-            s_off[e] = ot;
-            a.off[e] = ot;
-            if (c4[j]) {
-                if (a.use_tc) a.sub[(a.sg ? 1 : 0) + ou] = SubJob{e, ot, c4[j], 0};
-                a.used[ou++] = e;
-            }
-            ot += c4[j];
+        const int ot = bt + st - c, ou = bu + su - used;
+        s_off[e] = ot;
+        a.off[e] = ot;
+        if (c) {
+            if (a.use_tc) a.sub[(a.sg ? 1 : 0) + ou] = SubJob{e, ot, c, 0};
+            a.used[ou] = e;
         }
-        if (tid == blockDim.x - 1) {
-            a.off[kExperts] = ot;
-            a.hdr->n_pairs = ot;
-            a.hdr->n_used = ou;
-            if (a.use_tc) *a.n_sub = (a.sg ? 1 : 0) + ou;
+        if (tid == blockDim.x - 1) {  // totals: this thread's inclusive sums
+            a.off[kExperts] = ot + c;
+            a.hdr->n_pairs = ot + c;
+            a.hdr->n_used = ou + used;
+            if (a.use_tc) *a.n_sub = (a.sg ? 1 : 0) + ou + used;
         }
     }
     __syncthreads();
@@ -308,7 +292,9 @@ __global__ void __launch_bounds__(128) dec_router_kernel(DecArgs a) {
     if (lane == 0) s_inv[warp] = invalid;
     __syncthreads();
     if (tid == 0) {
-        a.hdr->invalid_tokens = s_inv[0] + s_inv[1] + s_inv[2] + s_inv[3];
+        int inv = 0;
+        for (int w = 0; w < kK1Threads / 32; w++) inv += s_inv[w];
+        a.hdr->invalid_tokens = inv;
         a.ctr->k1_ticket = 0;
     }
 }
@@ -764,7 +750,7 @@ int launch_k1(const DecArgs &a, cudaStream_t st, size_t smem) {
     auto k = dec_router_kernel<QG, TMAX>;
     int rc = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (rc) return rc;
-    return launch_pdl(k, dim3(a.k1_ctas), dim3(128), smem, st, true, a);
+    return launch_pdl(k, dim3(a.k1_ctas), dim3(kK1Threads), smem, st, true, a);
 }
 
 template <int QG, int QD>
