@@ -204,6 +204,11 @@ __device__ __forceinline__ void tmem_ld8_nw(uint32_t addr, uint32_t (&r)[8]) {
                  : "r"(addr));
 }
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ uint32_t tmem_ld1(uint32_t addr) {
+    uint32_t r;
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x1.b32 {%0}, [%1];" : "=r"(r) : "r"(addr));
+    return r;
+}
 // 32 consecutive columns of this thread's lane
 __device__ __forceinline__ void tmem_st32(uint32_t addr, const uint32_t (&r)[32]) {
     asm volatile(
@@ -285,10 +290,10 @@ __device__ __forceinline__ uint4 q4k_row_scales(const unsigned char *row) {
     return make_uint4(__float_as_uint(d), __float_as_uint(dmin), m4[0], m4[1]);
 }
 
-// sum_g m_g * xs[token][g] for tokens j and j+1 (xs: 8 group sums per token)
-__device__ __forceinline__ float2 mterm2(const float (&mg)[8], const float *xs, int j) {
-    const float4 a0 = *reinterpret_cast<const float4 *>(xs + j * 8), a1 = *reinterpret_cast<const float4 *>(xs + j * 8 + 4);
-    const float4 b0 = *reinterpret_cast<const float4 *>(xs + j * 8 + 8), b1 = *reinterpret_cast<const float4 *>(xs + j * 8 + 12);
+// sum_g m_g * xs[row][g] for rows j0 and j1 (xs: 8 group sums per row)
+__device__ __forceinline__ float2 mterm2(const float (&mg)[8], const float *xs, int j0, int j1) {
+    const float4 a0 = *reinterpret_cast<const float4 *>(xs + j0 * 8), a1 = *reinterpret_cast<const float4 *>(xs + j0 * 8 + 4);
+    const float4 b0 = *reinterpret_cast<const float4 *>(xs + j1 * 8), b1 = *reinterpret_cast<const float4 *>(xs + j1 * 8 + 4);
     float2 t = __fmul2_rn(make_float2(mg[0], mg[0]), make_float2(a0.x, b0.x));
     t = __ffma2_rn(make_float2(mg[1], mg[1]), make_float2(a0.y, b0.y), t);
     t = __ffma2_rn(make_float2(mg[2], mg[2]), make_float2(a0.z, b0.z), t);
@@ -610,8 +615,10 @@ __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a,
             // D columns c (hi) and kTok + c (lo): token c of all T tokens (gate/up on
             // per-token activations) or row c of the tile
             const bool by_tok = gu && a.all_tok;
-            const int ncol = by_tok ? ((T + 15) & ~15) : ((it.n + 15) & ~15);
-            const int hw = ncol >> 1;  // columns per half (multiple of 8)
+            // token slots j (the item's tokens, in order) split in two halves of hw
+            // (even) slots; slot j reads D column j, or column tok_j when the tile
+            // multiplied all T tokens
+            const int hw = ((it.n + 3) >> 2) << 1;
             const int j0 = half * hw;
             const int nsb = gu ? gu_sb : dn_sb;
             float2 acc[2][kHalf / 2];
@@ -644,17 +651,29 @@ __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a,
                         for (int cb = 0; cb < kHalf / 8; cb++) {
                             if (cb * 8 >= hw) break;
                             uint32_t rh[8], rl[8];
-                            tmem_ld8_nw(col0 + j0 + cb * 8, rh);
-                            tmem_ld8_nw(col0 + kTok + j0 + cb * 8, rl);
+                            if (by_tok) {  // gather the slots' token columns
+#pragma unroll
+                                for (int i = 0; i < 8; i++) {
+                                    const int c = tb.tok[min(j0 + cb * 8 + i, it.n - 1)];
+                                    rh[i] = tmem_ld1(col0 + c);
+                                    rl[i] = tmem_ld1(col0 + kTok + c);
+                                }
+                            } else {
+                                tmem_ld8_nw(col0 + j0 + cb * 8, rh);
+                                tmem_ld8_nw(col0 + kTok + j0 + cb * 8, rl);
+                            }
                             tmem_wait_ld();
 #pragma unroll
                             for (int pp = 0; pp < 4; pp++) {
+                                if (cb * 8 + 2 * pp >= hw) break;
                                 const int j = j0 + cb * 8 + 2 * pp;
+                                const int c0 = by_tok ? tb.tok[min(j, it.n - 1)] : j;
+                                const int c1 = by_tok ? tb.tok[min(j + 1, it.n - 1)] : j + 1;
                                 const float2 hi = make_float2(__uint_as_float(rh[2 * pp]), __uint_as_float(rh[2 * pp + 1]));
                                 const float2 lo = make_float2(__uint_as_float(rl[2 * pp]), __uint_as_float(rl[2 * pp + 1]));
-                                const float2 inv = make_float2(inv4[j * 4], inv4[j * 4 + 4]);
+                                const float2 inv = make_float2(inv4[c0 * 4], inv4[c1 * 4]);
                                 const float2 dot = __fmul2_rn(__ffma2_rn(lo, k2048, hi), inv);
-                                const float2 mt = mterm2(mg, xs, j);
+                                const float2 mt = mterm2(mg, xs, c0, c1);
                                 float2 &ac = acc[m][cb * 4 + pp];
                                 ac = __ffma2_rn(d2, dot, ac);
                                 ac = __ffma2_rn(nm2, mt, ac);
@@ -681,13 +700,14 @@ __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a,
                             tmem_wait_ld();
 #pragma unroll
                             for (int pp = 0; pp < 4; pp++) {
+                                if (cb * 8 + 2 * pp >= hw) break;
                                 const int j = j0 + cb * 8 + 2 * pp;
                                 const float2 v = __ffma2_rn(make_float2(__uint_as_float(rl[2 * pp]), __uint_as_float(rl[2 * pp + 1])), k2048,
                                                             make_float2(__uint_as_float(rh[2 * pp]), __uint_as_float(rh[2 * pp + 1])));
                                 const float2 dot = __fmul2_rn(v, make_float2(inv4[j * 4 + ioff + h], inv4[j * 4 + 4 + ioff + h]));
                                 float2 &ac = acc[0][cb * 4 + pp];
                                 ac = __ffma2_rn(d2, dot, ac);
-                                if (h) ac = __ffma2_rn(nm2, mterm2(mg, xs, j), ac);
+                                if (h) ac = __ffma2_rn(nm2, mterm2(mg, xs, j, j + 1), ac);
                             }
                         }
                     }
@@ -701,13 +721,14 @@ __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a,
             }
             ok = ok && wait_phase(&bars.tab_full[slot], (seq >> 2) & 1, &abort_flag, err);
             if (!bar_all(3, 256, ok)) break;
-            // the tile's outputs (SwiGLU for gate/up) to the shared buffer sv[token][row]
+            // the tile's outputs (SwiGLU for gate/up) to the shared buffer sv[slot][row]
             float *sv = reinterpret_cast<float *>(smem + kOffV);
 #pragma unroll
             for (int cb = 0; cb < kHalf / 8; cb++) {
                 if (cb * 8 < hw) {
 #pragma unroll
                     for (int pp = 0; pp < 4; pp++) {
+                        if (cb * 8 + 2 * pp >= hw) break;  // the other half's slots
                         float2 v = acc[0][cb * 4 + pp];
                         if (gu) {
                             const float2 u = acc[1][cb * 4 + pp];
@@ -727,7 +748,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a,
                 // scale from the tile's max |v|
 #pragma unroll 1
                 for (int j = ew; j < it.n; j += kEpiWarps) {
-                    const float *vj = sv + (by_tok ? tb.tok[j] : j) * kTcRows;
+                    const float *vj = sv + j * kTcRows;
                     const float v0 = vj[lane], v1 = vj[32 + lane], v2 = vj[64 + lane], v3 = vj[96 + lane];
                     float s0 = v0, s1 = v1, s2 = v2, s3 = v3;
 #pragma unroll
@@ -752,7 +773,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a,
                 // fp16 hi/lo split of v*s for the down tiles
 #pragma unroll 1
                 for (int j = et >> 7; j < it.n; j += 2) {
-                    const float v = sv[(by_tok ? tb.tok[j] : j) * kTcRows + rr] * s_scale[j];
+                    const float v = sv[j * kTcRows + rr] * s_scale[j];
                     const __half hi = __float2half_rn(v);
                     const size_t base = (size_t)tb.mrow[j] * 2 * F + it.mt * kTcRows + rr;
                     a.mid16[base] = hi;

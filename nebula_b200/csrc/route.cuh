@@ -37,45 +37,39 @@ __device__ __forceinline__ void route_token_warp(const float *logits, const floa
     }
     // Each lane keeps the best of its 16 values as an order-preserving key; a
     // pick is two warp reductions: the largest key, then the lowest index among
-    // the lanes holding it. Only the winning lane rescans its values.
+    // the lanes holding it. Only the winning lane rescans its values (a taken
+    // mask, so everything stays in registers). Lane k keeps pick k; every lane
+    // sums the weights in rank order.
     uint32_t key[16];
 #pragma unroll
     for (int m = 0; m < 16; m++) key[m] = float_key(v[m] + 0.0f);  // -0 ties with +0, as in the comparison
-    uint32_t bk = key[0];
+    uint32_t taken = 0, bk = key[0];
     int bm = 0;
 #pragma unroll
     for (int m = 1; m < 16; m++)
         if (key[m] > bk) bk = key[m], bm = m;
-    float sel_w[kTop];
-    int sel_id[kTop];
-    float largest = 0.0f;
-#pragma unroll
+    float largest = 0.0f, total = 0.0f, my_w = 0.0f;
+    int my_id = -1;
+#pragma unroll 1
     for (int k = 0; k < kTop; k++) {
         const uint32_t mk = __reduce_max_sync(0xffffffffu, bk);
         const int bi = (int)__reduce_min_sync(0xffffffffu, bk == mk ? (uint32_t)(bm * 32 + lane) : 0xFFFFu);
         const float bv = key_float(mk);
         if (k == 0) largest = bv;  // the first pick is the maximum of all 512
-        sel_id[k] = bi;
-        sel_w[k] = expf(bv - largest);
+        const float w = expf(bv - largest);
+        total += w;
+        if (lane == k) my_id = bi, my_w = w;
         if ((bi & 31) == lane) {
+            taken |= 1u << (bi >> 5);
+            bk = 0, bm = 0;
 #pragma unroll
             for (int m = 0; m < 16; m++)
-                if (m == (bi >> 5)) key[m] = 0;  // below every finite value
-            bk = key[0], bm = 0;
-#pragma unroll
-            for (int m = 1; m < 16; m++)
-                if (key[m] > bk) bk = key[m], bm = m;
+                if (!((taken >> m) & 1u) && key[m] > bk) bk = key[m], bm = m;
         }
     }
-    if (lane == 0) {
-        float total = 0.0f;
-#pragma unroll
-        for (int k = 0; k < kTop; k++) total += sel_w[k];
-#pragma unroll
-        for (int k = 0; k < kTop; k++) {
-            ids[k] = sel_id[k];
-            weights[k] = sel_w[k] / total;
-        }
+    if (lane < kTop) {
+        ids[lane] = my_id;
+        weights[lane] = my_w / total;
     }
 }
 }  // namespace nb
