@@ -125,6 +125,20 @@ int qg_moe_routed(float *out, const float *x, const int *ids, const float *weigh
                   const void *gate, int gate_type, const void *up, int up_type,
                   const void *down, int down_type, int hidden, int ffn, void *workspace);
 
+/* qg_moe_routed without a caller workspace (no counterpart in the reference):
+ * for callers that cannot allocate device memory where they call, e.g. a
+ * runtime whose device memory another allocator reserves in full up front.
+ * The library keeps one static 4 MiB scratch per device (a T <= 17 batch at
+ * hidden 2048 / ffn 512 fits); shapes whose qg_moe_workspace_bytes exceed it
+ * return cudaErrorInvalidValue before anything is launched. Nothing is
+ * allocated. The first call on a device looks the scratch up and zeroes it
+ * (and synchronises), so make it before any stream capture. Calls share the
+ * scratch: calls that overlap on the device (other streams, other host
+ * threads) race. */
+int qg_moe_routed_static(float *out, const float *x, const int *ids, const float *weights, int tokens,
+                         const void *gate, int gate_type, const void *up, int up_type,
+                         const void *down, int down_type, int hidden, int ffn);
+
 /* One whole MoE layer (qwen/qwen.c:714-735): router GEMV against the F32
  * router [512][hidden] with the reference lane order (so ids are bit-exact),
  * plus logit_bias[512] when non-NULL (a per-expert routing bias; the

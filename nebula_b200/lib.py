@@ -37,6 +37,7 @@ SIGNATURES = {
     "mtp_moe": ([P, P, P, P, P, P, I, P, I, P, I, I], I),
     "moe_workspace_bytes": ([I, I, I, C.POINTER(Z)], I),
     "moe_routed": ([P, P, P, P, I, P, I, P, I, P, I, I, I, P], I),
+    "moe_routed_static": ([P, P, P, P, I, P, I, P, I, P, I, I, I], I),
     "moe_layer": ([P, P, P, P, I, P, P, P, I, P, I, P, I, P, I, P, I, P, I, P, I, I, P], I),
     "moe_status": ([P, C.POINTER(I), C.POINTER(I), C.POINTER(I)], I),
     "moe_profile": ([I], I), "moe_profile_read": ([I, C.POINTER(D), C.POINTER(I)], I),
