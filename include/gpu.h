@@ -157,6 +157,36 @@ int qg_moe_layer(float *out, int *ids_out, float *weights_out, const float *x, i
                  const void *shared_down, int shared_down_type,
                  const float *shared_router, int hidden, int ffn, void *workspace);
 
+/* Expert parallelism across the GPUs of one box (no counterpart in the
+ * reference, which runs on one GPU): one process per GPU, every rank calls
+ * qg_moe_layer_ep for the same tokens and layer. Each rank holds n_local
+ * experts (gate/up/down as for qg_moe_layer, n_local of them) and
+ * expert_local[512] (device) gives each expert's index there, or -1 when
+ * another rank holds it; one rank (shared_rank) computes the shared expert.
+ * The router is replicated, so every rank derives the same ids; each rank
+ * computes its experts' weighted rows and stores them into every rank's
+ * workspace over NVLink, then every rank reduces all rows in router-rank
+ * order, so `out` on every rank is bitwise the single-GPU qg_moe_layer output.
+ * workspaces[r] is rank r's workspace (qg_ep_workspace_bytes, zero-filled
+ * once, allocated with qg_alloc) as seen from this process: this rank's own
+ * pointer and the others mapped with qg_ep_ipc_open from the 64-byte handles
+ * each rank exports with qg_ep_ipc_handle. Calls go in the same order on
+ * every rank; a rank that stops makes the others' combines time out (error
+ * bit 8 in qg_moe_status) instead of hanging. tokens <= 32, Q4_K only. */
+int qg_ep_workspace_bytes(int tokens, int hidden, int ffn, size_t *bytes);
+int qg_ep_ipc_handle(void *workspace, void *handle);
+int qg_ep_ipc_open(const void *handle, void **ptr);
+int qg_ep_ipc_close(void *ptr);
+int qg_moe_layer_ep(float *out, int *ids_out, float *weights_out, const float *x, int tokens,
+                    const float *router, const float *logit_bias,
+                    const void *gate, int gate_type, const void *up, int up_type,
+                    const void *down, int down_type, int n_local, const int *expert_local,
+                    const void *shared_gate, int shared_gate_type,
+                    const void *shared_up, int shared_up_type,
+                    const void *shared_down, int shared_down_type,
+                    const float *shared_router, int shared_rank, int hidden, int ffn,
+                    int rank, int ranks, void *const *workspaces);
+
 /* Reads the status words the last MoE call left in `workspace`:
  * invalid_tokens = tokens given NaN rows, selected = (token, expert) pairs
  * computed, experts = distinct experts used. Synchronises the device. */

@@ -27,6 +27,7 @@
 #include <algorithm>
 #include <cstddef>
 #include <utility>
+#include <cstring>
 #include <vector>
 #include "quant.cuh"
 #include "moe_decode.cuh"
@@ -1004,6 +1005,8 @@ DecArgs dec_args(int T, int H, int F, int gt, int dt, const float *x, float *out
     a.n_sub = reinterpret_cast<int *>(b + L.nsub);
     a.mid16 = reinterpret_cast<__half *>(b + L.mid16);
     a.midinv = reinterpret_cast<float *>(b + L.midinv);
+    a.n_experts = kExperts;
+    a.ep_shared_here = 1;
     return a;
 }
 
@@ -1121,4 +1124,170 @@ extern "C" int qg_moe_profile_read(int phase, double *total_ms, int *launches) {
     *total_ms = sum;
     *launches = n;
     return 0;
+}
+
+// ------------------------------------------------------------------ expert parallelism
+// One process per GPU. Every rank routes the same tokens (the router is
+// replicated and bit-exact, so all ranks agree on every id), runs the tiles of
+// the experts it holds, and writes each weighted slot row (and, on one rank,
+// the shared expert's rows) straight into every rank's workspace over NVLink.
+// Its last CTA then raises its flag in every rank. Each rank's combine kernel
+// waits for all flags of the call (bounded), reduces in router-rank order and
+// advances the call epoch; slot buffers alternate with the epoch's parity, so
+// a rank one layer ahead never overwrites rows a peer is still combining.
+namespace {
+
+struct EpLayout {
+    size_t slots, shout, flags, epoch, total;
+};
+
+EpLayout ep_layout(int T, int H, int F) {
+    EpLayout E{};
+    size_t p = align256(dec_layout(T, H, F).total);
+    auto take = [&](size_t bytes) {
+        size_t at = p;
+        p = align256(p + bytes);
+        return at;
+    };
+    E.slots = take(sizeof(float) * 2 * (size_t)T * kTop * H);  // [2][T*10][H]
+    E.shout = take(sizeof(float) * 2 * (size_t)T * H);         // [2][T][H]
+    E.flags = take(sizeof(int) * kMaxRanks);                     // epoch reached by each source rank
+    E.epoch = take(sizeof(int) * 2);                             // call epoch, combine ticket
+    E.total = p;
+    return E;
+}
+
+__device__ __forceinline__ int ld_acquire_sys(const int *p) {
+    int v;
+    asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// grid (H/256, T): out[t] = sum_k (rank order) slots[t][k] + sigmoid(g_t) * shared[t]
+// once every rank has raised its flag for this call.
+__global__ void ep_combine_kernel(float *out, const float *slots, const float *shout, const int *ids,
+                                  const int *expect, const float *sgate, int has_shared, int T, int H, int ranks,
+                                  const int *flags, int *epoch, int *err) {
+    __shared__ int s_ok;
+    const int t = blockIdx.y, d = blockIdx.x * blockDim.x + threadIdx.x;
+    const int e = __ldcg(epoch);
+    if (threadIdx.x == 0) {
+        int ok = 1;
+        const uint64_t t0 = global_ns();
+        for (int p = 0; p < ranks && ok; p++)
+            while (ld_acquire_sys(flags + p) < e + 1) {
+                if (global_ns() - t0 > kWaitLimitNs) {
+                    atomicOr(err, 8);
+                    ok = 0;
+                    break;
+                }
+                __nanosleep(100);
+            }
+        s_ok = ok;
+    }
+    __syncthreads();
+    if (s_ok && d < H) {
+        const size_t par = e & 1;
+        const bool bad = (__ldcg(expect + t) & (1 << 16)) != 0;
+        float sum = 0.0f;
+#pragma unroll
+        for (int k = 0; k < kTop; k++) {
+            const int id = __ldcg(ids + t * kTop + k);
+            sum += id >= 0 ? __ldcg(slots + ((par * T + t) * kTop + k) * H + d) : 0.0f;
+        }
+        if (has_shared) sum = __fmaf_rn(__ldcg(shout + (par * T + t) * H + d), sigmoidf_ref(__ldcg(sgate + t)), sum);
+        out[(size_t)t * H + d] = bad ? __int_as_float(0x7fc00000) : sum;
+    }
+    // the epoch advances once every CTA has read it
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();
+        if (atomicAdd(epoch + 1, 1) == (int)(gridDim.x * gridDim.y) - 1) {
+            epoch[1] = 0;
+            __threadfence();
+            epoch[0] = e + 1;
+        }
+    }
+}
+
+}  // namespace
+
+extern "C" int qg_ep_workspace_bytes(int tokens, int hidden, int ffn, size_t *bytes) {
+    if (!bytes || check_shape(tokens, hidden, ffn) || tokens > kMaxDecodeTokens) return cudaErrorInvalidValue;
+    *bytes = ep_layout(tokens, hidden, ffn).total;
+    return 0;
+}
+
+extern "C" int qg_ep_ipc_handle(void *workspace, void *handle) {
+    if (!workspace || !handle) return cudaErrorInvalidValue;
+    cudaIpcMemHandle_t h;
+    int rc = cudaIpcGetMemHandle(&h, workspace);
+    if (rc) return rc;
+    memcpy(handle, &h, sizeof(h));
+    return 0;
+}
+
+extern "C" int qg_ep_ipc_open(const void *handle, void **ptr) {
+    if (!handle || !ptr) return cudaErrorInvalidValue;
+    cudaIpcMemHandle_t h;
+    memcpy(&h, handle, sizeof(h));
+    return cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess);
+}
+
+extern "C" int qg_ep_ipc_close(void *ptr) { return ptr ? cudaIpcCloseMemHandle(ptr) : cudaErrorInvalidValue; }
+
+extern "C" int qg_moe_layer_ep(float *out, int *ids_out, float *weights_out, const float *x, int tokens,
+                               const float *router, const float *logit_bias, const void *gate, int gt, const void *up,
+                               int ut, const void *down, int dt, int n_local, const int *expert_local, const void *sg,
+                               int sgt, const void *su, int sut, const void *sd, int sdt, const float *s_router,
+                               int shared_rank, int hidden, int ffn, int rank, int ranks, void *const *workspaces) {
+    if (check_shape(tokens, hidden, ffn) || !router || !workspaces || !expert_local || (sg && !s_router))
+        return cudaErrorInvalidValue;
+    if (ranks < 1 || ranks > kMaxRanks || rank < 0 || rank >= ranks || shared_rank < 0 || shared_rank >= ranks ||
+        n_local < 1 || n_local > kExperts)
+        return cudaErrorInvalidValue;
+    if (gt != 12 || ut != 12 || dt != 12 || (sg && (sgt != 12 || sut != 12 || sdt != 12)) ||
+        !dec_supported(tokens, hidden, ffn, gt, dt) || !tc_supported(hidden, ffn, gt, dt))
+        return cudaErrorNotSupported;  // expert parallelism runs on the Q4_K tensor-core path
+    void *workspace = workspaces[rank];
+    for (int p = 0; p < ranks; p++)
+        if (!workspaces[p]) return cudaErrorInvalidValue;
+    if (!out || !x || !gate || !up || !down || !dec_pointers_ok(gate, up, down, x, out, workspace) ||
+        !aligned16(router) || (sg && (!su || !sd || !aligned16(sg) || !aligned16(su) || !aligned16(sd) ||
+                                      !aligned16(s_router))))
+        return cudaErrorInvalidValue;
+    cudaStream_t st = launch_stream;
+    const DecLayout DL = dec_layout(tokens, hidden, ffn);
+    const EpLayout EL = ep_layout(tokens, hidden, ffn);
+    char *b = static_cast<char *>(workspace);
+    int *ids = ids_out ? ids_out : reinterpret_cast<int *>(b + DL.ids);
+    float *wts = weights_out ? weights_out : reinterpret_cast<float *>(b + DL.wts);
+    DecArgs a = dec_args(tokens, hidden, ffn, gt, dt, x, out, ids, wts, workspace);
+    a.router = router;
+    a.bias = logit_bias;
+    a.s_router = sg ? s_router : nullptr;
+    a.gate = static_cast<const unsigned char *>(gate);
+    a.up = static_cast<const unsigned char *>(up);
+    a.down = static_cast<const unsigned char *>(down);
+    a.sg = static_cast<const unsigned char *>(sg);
+    a.su = static_cast<const unsigned char *>(su);
+    a.sd = static_cast<const unsigned char *>(sd);
+    a.ep_local = expert_local;
+    a.n_experts = n_local;
+    a.ep_shared_here = rank == shared_rank;
+    a.ep_ranks = ranks, a.ep_rank = rank;
+    for (int p = 0; p < ranks; p++) {
+        char *pb = static_cast<char *>(workspaces[p]);
+        a.ep_slots[p] = reinterpret_cast<float *>(pb + EL.slots);
+        a.ep_shout[p] = reinterpret_cast<float *>(pb + EL.shout);
+        a.ep_flags[p] = reinterpret_cast<int *>(pb + EL.flags);
+    }
+    a.ep_epoch = reinterpret_cast<int *>(b + EL.epoch);
+    int rc = dec_run_timed(a, st);
+    if (rc) return rc;
+    ep_combine_kernel<<<dim3((hidden + 255) / 256, tokens), 256, 0, st>>>(
+        out, reinterpret_cast<const float *>(b + EL.slots), reinterpret_cast<const float *>(b + EL.shout), ids,
+        a.expect, a.sgate, sg != nullptr, tokens, hidden, ranks, reinterpret_cast<const int *>(b + EL.flags),
+        reinterpret_cast<int *>(b + EL.epoch), &a.hdr->error);
+    return cudaGetLastError();
 }

@@ -191,7 +191,7 @@ __global__ void __launch_bounds__(kK1Threads) dec_router_kernel(DecArgs a) {
     __shared__ unsigned s_bm[kExperts];
     __shared__ int s_off[kExperts];
     __shared__ int s_bad[kMaxDecodeTokens];
-    __shared__ int s_wt[kK1Threads / 32], s_wu[kK1Threads / 32], s_inv[kK1Threads / 32];
+    __shared__ int s_wt[kK1Threads / 32], s_wu[kK1Threads / 32], s_wm[kK1Threads / 32], s_inv[kK1Threads / 32];
     if (a.router) {
         for (int t = warp; t < T; t += blockDim.x / 32)
             route_token_warp(a.logits + t * kExperts, a.bias, a.ids + t * kTop, a.wts + t * kTop);
@@ -228,37 +228,42 @@ __global__ void __launch_bounds__(kK1Threads) dec_router_kernel(DecArgs a) {
         static_assert(kK1Threads == kExperts, "one expert per thread");
         const int e = tid;
         const int c = __popc(s_bm[e]), used = c > 0;
-        int st = c, su = used;
+        const int loc = a.ep_local ? __ldg(a.ep_local + e) : e;  // index in gate/up/down, or -1
+        const int mine = used && loc >= 0;
+        int st = c, su = used, sm = mine;
 #pragma unroll
         for (int d = 1; d < 32; d <<= 1) {
-            const int vt = __shfl_up_sync(0xffffffffu, st, d), vu = __shfl_up_sync(0xffffffffu, su, d);
+            const int vt = __shfl_up_sync(0xffffffffu, st, d), vu = __shfl_up_sync(0xffffffffu, su, d),
+                      vm = __shfl_up_sync(0xffffffffu, sm, d);
             if (lane >= d) {
                 st += vt;
                 su += vu;
+                sm += vm;
             }
         }
         if (lane == 31) {
             s_wt[warp] = st;
             s_wu[warp] = su;
+            s_wm[warp] = sm;
         }
         __syncthreads();
-        int bt = 0, bu = 0;
+        int bt = 0, bu = 0, bmn = 0;
         for (int w = 0; w < warp; w++) {
             bt += s_wt[w];
             bu += s_wu[w];
+            bmn += s_wm[w];
         }
-        const int ot = bt + st - c, ou = bu + su - used;
+        const int ot = bt + st - c, ou = bu + su - used, om = bmn + sm - mine;
+        const int shared_sub = (a.sg && a.ep_shared_here) ? 1 : 0;
         s_off[e] = ot;
         a.off[e] = ot;
-        if (c) {
-            if (a.use_tc) a.sub[(a.sg ? 1 : 0) + ou] = SubJob{e, ot, c, 0};
-            a.used[ou] = e;
-        }
+        if (c) a.used[ou] = e;
+        if (mine && a.use_tc) a.sub[shared_sub + om] = SubJob{loc, ot, c, 0};
         if (tid == blockDim.x - 1) {  // totals: this thread's inclusive sums
             a.off[kExperts] = ot + c;
             a.hdr->n_pairs = ot + c;
             a.hdr->n_used = ou + used;
-            if (a.use_tc) *a.n_sub = (a.sg ? 1 : 0) + ou + used;
+            if (a.use_tc) *a.n_sub = shared_sub + om + mine;
         }
     }
     __syncthreads();
@@ -272,7 +277,7 @@ __global__ void __launch_bounds__(kK1Threads) dec_router_kernel(DecArgs a) {
         // counters the tensor-core kernel counts up from zero
         for (int i = tid; i <= kExperts; i += blockDim.x) a.ctr->gu_done[i] = 0;
         for (int i = tid; i < T * (H / kTcRows); i += blockDim.x) a.ctr->tilecnt[i] = 0;
-        if (tid == 0 && has_shared) a.sub[0] = SubJob{-1, 0, T, 0};
+        if (tid == 0 && has_shared && a.ep_shared_here) a.sub[0] = SubJob{-1, 0, T, 0};
     }
     int invalid = 0;
     for (int t = tid; t < T; t += blockDim.x) {
@@ -282,7 +287,7 @@ __global__ void __launch_bounds__(kK1Threads) dec_router_kernel(DecArgs a) {
         const int expect = n + has_shared;
         a.expect[t] = expect | (s_bad[t] ? (int)kBadBit : 0);
         invalid += s_bad[t];
-        if (expect == 0) {  // no contribution will arrive: write the row here
+        if (expect == 0 && !a.ep_ranks) {  // no contribution will arrive: write the row here
             const float v = s_bad[t] ? __int_as_float(0x7fc00000) : 0.0f;
             for (int d = 0; d < H; d++) a.out[(size_t)t * H + d] = v;
         }
@@ -859,12 +864,16 @@ int dec_run(const DecArgs &in, cudaStream_t st, cudaEvent_t split) {
         t.all_tok = 1;
         t.x16 = a.x16, t.xinv = a.xinv, t.xsum = a.xsum;
         t.mi_stride = ((a.F / 128) + 3) & ~3;
-        t.sub = a.sub, t.n_sub = a.n_sub, t.shared_subs = a.sg ? 1 : 0;
+        t.sub = a.sub, t.n_sub = a.n_sub, t.shared_subs = (a.sg && a.ep_shared_here) ? 1 : 0;
         t.pairs = a.pairs, t.wts = a.wts, t.ids = a.ids, t.expect = a.expect, t.sgate = a.sg ? a.sgate : nullptr;
         t.mid16 = a.mid16, t.midinv = a.midinv, t.msum = a.msum;
         t.slots = a.slots, t.shout = a.shout, t.out = a.out;
         t.queue = &a.ctr->tc_queue, t.tc_ticket = &a.ctr->tc_ticket;
         t.gu_done = a.ctr->gu_done, t.tilecnt = a.ctr->tilecnt, t.err = &a.hdr->error;
+        t.n_experts = a.n_experts;
+        t.ep_ranks = a.ep_ranks, t.ep_rank = a.ep_rank, t.ep_epoch = a.ep_epoch;
+        for (int p = 0; p < kMaxRanks; p++)
+            t.ep_slots[p] = a.ep_slots[p], t.ep_shout[p] = a.ep_shout[p], t.ep_flags[p] = a.ep_flags[p];
         TcMaps maps;
         if ((rc = tc_make_maps(t, maps, kMaxDecodeTokens))) return rc;
         return tc_launch(t, maps, st, pdl, kMaxDecodeTokens);

@@ -46,6 +46,15 @@ struct DecArgs {
     float *xinv, *midinv;
     SubJob *sub;
     int *n_sub;
+    // expert parallelism: ep_local[e] = index of expert e in gate/up/down on
+    // this rank, or -1 (another rank's); null = all 512 here
+    const int *ep_local;
+    int n_experts;       // experts in gate/up/down
+    int ep_shared_here;  // this rank computes the shared expert
+    int ep_ranks, ep_rank;
+    float *ep_slots[kMaxRanks], *ep_shout[kMaxRanks];
+    int *ep_flags[kMaxRanks];
+    int *ep_epoch;
     // filled by dec_run
     int gstride, dn_rows, stage_bytes, k1_ctas;
 };

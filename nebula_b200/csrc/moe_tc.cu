@@ -784,6 +784,21 @@ __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a,
                 if (et == 0) atomicAdd(a.gu_done + it.sub, 1);
             } else {
                 const int row = it.mt * kTcRows + rr;
+                if (a.ep_ranks) {
+                    // every rank's buffers for this call's parity; the combine kernel reduces
+                    const int par = __ldcg(a.ep_epoch) & 1;
+#pragma unroll 1
+                    for (int j = et >> 7; j < it.n; j += 2) {
+                        const float y = sv[j * kTcRows + rr];
+                        const size_t o = it.expert < 0 ? ((size_t)par * T + tb.tok[j]) * H + row
+                                                       : ((size_t)par * T * kTop + tb.slot[j]) * H + row;
+                        const float v = it.expert < 0 ? y : y * tb.w[j];
+                        for (int p = 0; p < a.ep_ranks; p++) (it.expert < 0 ? a.ep_shout[p] : a.ep_slots[p])[o] = v;
+                    }
+                    __syncwarp();
+                    if (lane == 0) arrive(&bars.item_empty[slot]);
+                    continue;
+                }
 #pragma unroll 1
                 for (int j = et >> 7; j < it.n; j += 2) {
                     const float y = sv[j * kTcRows + rr];
@@ -833,11 +848,19 @@ __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a,
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem));
     }
     if (tid == 0) {
-        __threadfence();
+        if (a.ep_ranks) __threadfence_system();  // this CTA's peer stores before the ticket
+        else __threadfence();
         if (atomicAdd(a.tc_ticket, 1) == (int)gridDim.x - 1) {
-            __threadfence();
+            __threadfence_system();
             *a.queue = 0;
             *a.tc_ticket = 0;
+            if (a.ep_ranks) {  // every rank may now combine this rank's rows of this call
+                grid_dep_wait();
+                const int done = __ldcg(a.ep_epoch) + 1;
+                for (int p = 0; p < a.ep_ranks; p++)
+                    asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(a.ep_flags[p] + a.ep_rank), "r"(done)
+                                 : "memory");
+            }
         }
     }
 }
@@ -923,7 +946,7 @@ bool tc_supported(int H, int F, int QG, int QD) {
 size_t tc_smem_bytes() { return Cfg<kTcTok>::kSmem; }
 
 int tc_make_maps(const TcArgs &a, TcMaps &m, int tok) {
-    const size_t E = kExperts, H = a.H, F = a.F;
+    const size_t E = a.n_experts > 0 ? a.n_experts : kExperts, H = a.H, F = a.F;
     const size_t rows = (size_t)a.T * kTop + a.T;        // routed pairs + shared tokens
     const size_t xrows = a.all_tok ? (size_t)a.T : rows;  // rows of the gate/up activations
     const auto f16 = CU_TENSOR_MAP_DATA_TYPE_FLOAT16, f32 = CU_TENSOR_MAP_DATA_TYPE_FLOAT32;

@@ -7,6 +7,7 @@ namespace nb {
 
 constexpr int kTcTok = 48;     // tokens per sub-job (token tile of one expert)
 constexpr int kTcRows = 128;   // weight rows per tile (MMA M)
+constexpr int kMaxRanks = 8;   // expert-parallel ranks (GPUs of one box)
 
 // One token tile of one expert. expert < 0 is the shared expert, whose tokens
 // are tok0 .. tok0+n-1; a routed sub-job covers pairs[first .. first+n).
@@ -46,6 +47,16 @@ struct TcArgs {
     int *gu_done;          // [n_sub] finished gate/up tiles, zeroed by the planner
     int *tilecnt;          // [T][H/128], zeroed by the planner
     int *err;
+    int n_experts;         // experts held in gate/up/down
+    // Expert parallelism (ep_ranks > 0): the down tiles write their weighted
+    // rows into every rank's buffers (peer memory, double-buffered by the
+    // parity of the call epoch) instead of combining, and the last CTA raises
+    // this rank's flag in every rank; a separate combine kernel reduces.
+    int ep_ranks, ep_rank;
+    float *ep_slots[kMaxRanks];   // per rank: [2][T*10][H]
+    float *ep_shout[kMaxRanks];   // per rank: [2][T][H]
+    int *ep_flags[kMaxRanks];     // per rank: [kMaxRanks] epoch reached by each source rank
+    const int *ep_epoch;          // this rank's call epoch (advanced by the combine)
 };
 
 struct TcMaps {

@@ -39,6 +39,9 @@ SIGNATURES = {
     "moe_routed": ([P, P, P, P, I, P, I, P, I, P, I, I, I, P], I),
     "moe_routed_static": ([P, P, P, P, I, P, I, P, I, P, I, I, I], I),
     "moe_layer": ([P, P, P, P, I, P, P, P, I, P, I, P, I, P, I, P, I, P, I, P, I, I, P], I),
+    "ep_workspace_bytes": ([I, I, I, C.POINTER(Z)], I), "ep_ipc_handle": ([P, P], I),
+    "ep_ipc_open": ([P, C.POINTER(P)], I), "ep_ipc_close": ([P], I),
+    "moe_layer_ep": ([P, P, P, P, I, P, P, P, I, P, I, P, I, I, P, P, I, P, I, P, I, P, I, I, I, I, I, P], I),
     "moe_status": ([P, C.POINTER(I), C.POINTER(I), C.POINTER(I)], I),
     "moe_profile": ([I], I), "moe_profile_read": ([I, C.POINTER(D), C.POINTER(I)], I),
     "synth_weights": ([P, I, I, I, U64, F], I), "synth_normal": ([P, Z, U64, F], I),

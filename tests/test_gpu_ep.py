@@ -1,0 +1,88 @@
+"""Expert parallelism on two GPUs (one process each): every rank's
+qg_moe_layer_ep output equals the single-GPU qg_moe_layer output bit for bit,
+over three calls (both parities of the double-buffered slot rows), with the
+experts placed in snake order of a skewed ranking. Skipped on a machine with
+fewer than two GPUs."""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+H, F, T = 2048, 512, 17
+QROW_H, QROW_F = H // 256 * 144, F // 256 * 144  # Q4_K row bytes
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, results):
+    import torch
+    import torch.distributed as dist
+    torch.cuda.set_device(rank)
+    os.environ["MASTER_ADDR"], os.environ["MASTER_PORT"] = "127.0.0.1", str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from nebula_b200 import ep
+        from nebula_b200 import lib as L
+        L.load()
+        # identical weights and inputs on every rank
+        gate, up = L.synth_weights(12, 512 * F, H, 901), L.synth_weights(12, 512 * F, H, 902)
+        down = L.synth_weights(12, 512 * H, F, 903)
+        router = L.synth_weights(0, 512, H, 904)
+        sg, su = L.synth_weights(12, F, H, 905), L.synth_weights(12, F, H, 906)
+        sd, sr = L.synth_weights(12, H, F, 907), L.synth_weights(0, 1, H, 908)
+        rng = np.random.default_rng(11)
+        ranking = rng.permutation(512)
+        bias = np.zeros(512, np.float32)
+        bias[ranking] = (-1.1 * np.log(np.arange(1, 513))).astype(np.float32)
+        dbias = L.Device(bias)
+        owner = ep.snake_owner(ranking, world)
+        loc, experts = ep.local_map(owner, rank)
+        lgate = ep.extract_experts(gate, experts, F, QROW_H)
+        lup = ep.extract_experts(up, experts, F, QROW_H)
+        ldown = ep.extract_experts(down, experts, H, QROW_F)
+        dloc = L.Device(loc)
+        grp = ep.EpGroup(T, H, F, rank, world)
+        ws = L.workspace(T, H, F)
+        errors = []
+        for call in range(3):
+            x = L.Device(np.random.default_rng(100 + call).normal(0, 1, (T, H)).astype(np.float32))
+            ref = L.Device.empty((T, H), np.float32)
+            L.call("moe_layer", ref.p, None, None, x.p, T, router.p, dbias.p, gate.p, 12, up.p, 12, down.p, 12,
+                   sg.p, 12, su.p, 12, sd.p, 12, sr.p, H, F, ws.p)
+            out = L.Device.empty((T, H), np.float32)
+            L.call("moe_layer_ep", out.p, None, None, x.p, T, router.p, dbias.p, lgate.p, 12, lup.p, 12, ldown.p, 12,
+                   len(experts), dloc.p, sg.p, 12, su.p, 12, sd.p, 12, sr.p, call % world, H, F, rank, world,
+                   grp.ptrs)
+            a, b = ref.get(), out.get()
+            if not np.array_equal(a.view(np.uint32), b.view(np.uint32)):
+                errors.append(f"call {call}: {int((a != b).sum())} values differ, max |d| "
+                              f"{float(np.nanmax(np.abs(a - b)))}")
+        import ctypes as C
+        inv, sel, used = C.c_int(), C.c_int(), C.c_int()
+        L.call("moe_status", grp.ws.p, C.byref(inv), C.byref(sel), C.byref(used))
+        dist.barrier()
+        grp.close()
+        results[rank] = "; ".join(errors) if errors else "ok"
+    except Exception as e:  # reported to the parent
+        results[rank] = f"exception: {e!r}"
+    finally:
+        dist.destroy_process_group()
+
+
+def test_expert_parallel_matches_single_gpu():
+    import torch
+    world = 2
+    if torch.cuda.device_count() < world:
+        pytest.skip("needs two GPUs")
+    mgr = mp.get_context("spawn").Manager()
+    results = mgr.dict()
+    mp.start_processes(_worker, args=(world, _free_port(), results), nprocs=world, start_method="spawn", join=True)
+    assert [results.get(r) for r in range(world)] == ["ok"] * world, dict(results)
