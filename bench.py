@@ -19,10 +19,12 @@ top-10), `roofline` (dominant kernel vs measured HBM copy bandwidth),
 (the same metric through the C ABI with pinned host buffers copied in and
 results read back every step).
 
-Multi-GPU: launched by torch.distributed.run, one process per GPU. Until the
-expert-parallel path lands each rank runs an independent replica of the
-stack on its own tokens (weak scaling); the value is the sum over ranks of
-tokens processed divided by the slowest rank's time.
+Multi-GPU: launched by torch.distributed.run, one process
+per GPU, expert parallel. Every rank holds 1/N of each layer's experts (snake
+order of the layer's hot-expert ranking) plus the replicated router and shared
+expert, and all ranks run the same T tokens (strong scaling): each computes its
+experts' rows, stores them into every rank's workspace over NVLink and reduces.
+The value is T tokens per step divided by the slowest rank's step time.
 """
 from __future__ import annotations
 
@@ -119,28 +121,53 @@ class Clocks:
 
 
 class Stack:
-    """48 resident layers on the device plus per-layer inputs and outputs."""
+    """48 resident layers on the device plus per-layer inputs and outputs.
 
-    def __init__(self, L, layers: int, T: int, seed0: int = 0):
-        self.L, self.T, self.layers = L, T, layers
+    With ``ep=(rank, world)`` the rank keeps only its share of each layer's
+    experts (snake order of the layer's hot-expert ranking) and runs the
+    expert-parallel layer; weights and inputs are the same on every rank."""
+
+    def __init__(self, L, layers: int, T: int, seed0: int = 0, ep=None):
+        self.L, self.T, self.layers, self.ep = L, T, layers, ep
         self.w = []
+        if ep:
+            from nebula_b200 import ep as epm
+            rank, world = ep
+            self.epg = epm.EpGroup(T, H, F, rank, world)
         for l in range(layers):
             s = seed0 + 100 * l
-            d = {
-                "gate": L.synth_weights(Q4K, E * F, H, s + 1), "up": L.synth_weights(Q4K, E * F, H, s + 2),
-                "down": L.synth_weights(Q4K, E * H, F, s + 3), "router": L.synth_weights(0, E, H, s + 4),
+            d = {"router": L.synth_weights(0, E, H, s + 4)}
+            if ep:
+                owner = epm.snake_owner(np.random.default_rng(1000 + l).permutation(E), world)
+                loc, experts = epm.local_map(owner, rank)
+                for name, rows, cols, seed in (("gate", F, H, s + 1), ("up", F, H, s + 2), ("down", H, F, s + 3)):
+                    full = L.synth_weights(Q4K, E * rows, cols, seed)
+                    d[name] = epm.extract_experts(full, experts, rows, cols // 256 * 144)
+                    full.free()
+                d["local"], d["experts"], d["n_local"] = L.Device(loc), set(experts), len(experts)
+            else:
+                d.update({"gate": L.synth_weights(Q4K, E * F, H, s + 1), "up": L.synth_weights(Q4K, E * F, H, s + 2),
+                          "down": L.synth_weights(Q4K, E * H, F, s + 3)})
+            d.update({
                 "sg": L.synth_weights(Q4K, F, H, s + 5), "su": L.synth_weights(Q4K, F, H, s + 6),
                 "sd": L.synth_weights(Q4K, H, F, s + 7), "sr": L.synth_weights(0, 1, H, s + 8),
                 "bias": L.Device(zipf_bias(l)),
                 "x": L.synth_normal(T * H, 2 + l + 7919 * seed0),
                 "out": L.Device.empty((T, H), np.float32),
                 "ids": L.Device.empty((T, K), np.int32), "wts": L.Device.empty((T, K), np.float32),
-            }
+            })
             self.w.append(d)
-        self.ws = L.workspace(T, H, F)
+        self.ws = self.epg.ws if ep else L.workspace(T, H, F)
 
     def run_layer(self, l: int, x_ptr=None, out_ptr=None):
         d, L = self.w[l], self.L
+        if self.ep:
+            rank, world = self.ep
+            L.call("moe_layer_ep", out_ptr or d["out"].p, d["ids"].p, d["wts"].p, x_ptr or d["x"].p, self.T,
+                   d["router"].p, d["bias"].p, d["gate"].p, Q4K, d["up"].p, Q4K, d["down"].p, Q4K, d["n_local"],
+                   d["local"].p, d["sg"].p, Q4K, d["su"].p, Q4K, d["sd"].p, Q4K, d["sr"].p, l % world, H, F, rank,
+                   world, self.epg.ptrs)
+            return
         L.call("moe_layer", out_ptr or d["out"].p, d["ids"].p, d["wts"].p, x_ptr or d["x"].p, self.T,
                d["router"].p, d["bias"].p, d["gate"].p, Q4K, d["up"].p, Q4K, d["down"].p, Q4K,
                d["sg"].p, Q4K, d["su"].p, Q4K, d["sd"].p, Q4K, d["sr"].p, H, F, self.ws.p)
@@ -162,7 +189,12 @@ class Stack:
         return g
 
     def experts_used(self) -> list[int]:
-        return [len(np.unique(d["ids"].get())) for d in self.w]
+        """Experts this rank computed per layer (its share under expert parallelism)."""
+        out = []
+        for d in self.w:
+            u = set(np.unique(d["ids"].get()).tolist()) - {-1}
+            out.append(len(u & d["experts"]) if self.ep else len(u))
+        return out
 
 
 def cpu_reference_sample(L, stack: Stack | None, T: int, layers_sample: int, seconds: float, threads: int):
@@ -270,7 +302,8 @@ def main() -> None:
     from nebula_b200 import lib as L
     L.load()
     T = args.tokens
-    stack = Stack(L, args.layers, T, seed0=rank)
+    ep_mode = world > 1
+    stack = Stack(L, args.layers, T, seed0=0, ep=(rank, world) if ep_mode else None)
     L.call("sync")
     graph = stack.capture()
 
@@ -298,7 +331,7 @@ def main() -> None:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
     ms_step = ms / args.steps
-    value = T * world * args.steps / (ms / 1e3)
+    value = T * args.steps / (ms / 1e3)  # every rank works on the same T tokens
 
     # roofline: per-phase event timing over an eager replay of the same steps
     L.call("moe_profile", 1)
@@ -316,7 +349,8 @@ def main() -> None:
     # algorithmic bytes per launch: every used expert's gate/up/down rows (+ the
     # shared expert) read once, x read, out written; router: its matrix and x
     u_mean = float(np.mean(used))
-    alg_bytes = {"experts": (u_mean + 1) * EXPERT_BYTES + 2 * T * H * 4,
+    shared_share = 1.0 / world  # the shared expert runs on one rank per layer
+    alg_bytes = {"experts": (u_mean + shared_share) * EXPERT_BYTES + 2 * T * H * 4,
                  "decode_router": (E + 1) * H * 4 + T * H * 4 + T * K * 8}
     timed = {k: v for k, v in prof.items() if v[1] > 0 and k in alg_bytes}
     dom = max(timed, key=lambda k: timed[k][0])
@@ -352,11 +386,11 @@ def main() -> None:
         t = torch.tensor([e2e_s], device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_s = float(t.item())
-    e2e_value = T * world * args.steps / e2e_s
+    e2e_value = T * args.steps / e2e_s
 
     # prefill (config 4) on layer 0's weights
     prefill = None
-    if not args.no_prefill and rank == 0:
+    if not args.no_prefill and world == 1:  # config 4 is a single-GPU layer
         P = 2048
         rng = np.random.default_rng(3)
         dl = L.Device(rng.normal(0, 1, (P, E)).astype(np.float32))
@@ -392,7 +426,7 @@ def main() -> None:
                    "path": "tcgen05 tensor-core expert kernel (Q4_K codes and fp16 hi/lo activations)"}
 
     cpu = None
-    if not args.no_cpu and rank == 0:
+    if not args.no_cpu and world == 1:
         from oracle import oracle as orc
         threads = orc.host_threads()
         res = cpu_reference_sample(L, stack, T, 2, args.cpu_seconds, threads)
@@ -404,12 +438,12 @@ def main() -> None:
     line = {
         "metric": "moe_verify_tokens_per_s", "value": value, "unit": "tokens/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": f"48-layer routed-MoE stack (BASELINE config 3; config 5 at N>1), T={T} verify "
-                               "tokens per GPU, H=2048 F=512, 512 Q4_K experts/layer + Q4_K shared expert, "
-                               "top-10, Zipf-skewed routing",
-                   "layers": args.layers, "tokens_per_gpu": T,
-                   "parallelism": "replicas" if world > 1 else "single",
+        "scaling": "strong" if ep_mode else "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"48-layer routed-MoE stack (BASELINE config 3; config 5, expert parallel over "
+                               f"{world} GPUs, at N>1), T={T} verify tokens, H=2048 F=512, 512 Q4_K experts/layer "
+                               "+ Q4_K shared expert, top-10, Zipf-skewed routing",
+                   "layers": args.layers, "tokens": T,
+                   "parallelism": f"ep{world}" if ep_mode else "single",
                    "l2": "inputs larger than L2 (43.5 GB of weights streamed per step)",
                    "experts_used_per_layer_mean": float(np.mean(used)),
                    "stack_bytes_per_step": stack_bytes,
@@ -432,6 +466,8 @@ def main() -> None:
         print(json.dumps(line), flush=True)
     L.load().qg_graph_destroy(graph)
     if dist:
+        dist.barrier()
+        stack.epg.close()  # unmap the peers' workspaces before any rank frees its own
         dist.barrier()
         dist.destroy_process_group()
 

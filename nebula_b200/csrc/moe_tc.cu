@@ -338,7 +338,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a,
             mbar_init(&bars.item_full[i], 1);
             mbar_init(&bars.item_empty[i], 2 + 1 + kConvWarps + kEpiWarps);  // issuers, stager, converters, epilogue
             mbar_init(&bars.tab_full[i], 1);
-            mbar_init(&bars.sc_full[i], 4 + 1);  // low-nibble converters (row scales), stager (group sums, 1/s)
+            mbar_init(&bars.sc_full[i], kConvWarps + 1);  // converters (row scales), stager (group sums, 1/s)
             mbar_init(&bars.sc_empty[i], kEpiWarps);
         }
         for (int i = 0; i < kRawStages; i++) {
@@ -563,29 +563,40 @@ __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a,
                 const int st = gsb % kRawStages, sc_slot = gsb & 3;
                 if (!(ok = wait_phase(&bars.raw_full[st], (gsb / kRawStages) & 1, &abort_flag, err))) break;
                 const unsigned char *raw = smem + kOffRaw + st * kRawStage;
-                if (nib == 0) {
-                    if (gsb >= 4 && !(ok = wait_phase(&bars.sc_empty[sc_slot], ((gsb >> 2) - 1) & 1, &abort_flag, err)))
-                        break;
+                // row scales: matrix nib (gate by the low-nibble warps, up by the high-nibble ones)
+                if (gsb >= 4 && !(ok = wait_phase(&bars.sc_empty[sc_slot], ((gsb >> 2) - 1) & 1, &abort_flag, err)))
+                    break;
+                if (nib < mats) {
                     uint4 *scs = reinterpret_cast<uint4 *>(smem + kOffSc + sc_slot * kScSlot);
-                    for (int m = 0; m < mats; m++) scs[m * kTcRows + ct] = q4k_row_scales(raw + m * kSbBytes + ct * 144);
-                    __syncwarp();
-                    if (lane == 0) arrive(&bars.sc_full[sc_slot]);
+                    scs[nib * kTcRows + ct] = q4k_row_scales(raw + nib * kSbBytes + ct * 144);
                 }
-                for (int c = 0; c < 4; c++, gch++) {
-                    const int ab = gch % kAStages;
-                    if (gch >= kAStages &&
-                        !(ok = wait_phase(&bars.a_empty[ab], (gch / kAStages - 1) & 1, &abort_flag, err)))
-                        break;
+                __syncwarp();
+                if (lane == 0) arrive(&bars.sc_full[sc_slot]);
+                // kGrp chunks per store-completion wait (half the A ring)
+                constexpr int kGrp = kAStages >= 4 ? 2 : 1;
+                for (int c = 0; c < 4 && ok; c += kGrp, gch += kGrp) {
+                    for (int h = 0; h < kGrp; h++) {
+                        const int g = gch + h, ab = g % kAStages;
+                        if (g >= kAStages &&
+                            !(ok = wait_phase(&bars.a_empty[ab], (g / kAStages - 1) & 1, &abort_flag, err)))
+                            break;
+                    }
+                    if (!ok) break;
                     tc_fence_after();
-                    for (int m = 0; m < mats; m++) {
-                        uint32_t r[16];
-                        q4k_half_cols(raw + m * kSbBytes + ct * 144, c, nib, r);
-                        tmem_st16(a_lanes + (uint32_t)((ab * 2 + m) * 32), r);
+#pragma unroll
+                    for (int h = 0; h < kGrp; h++) {
+                        const int ab = (gch + h) % kAStages;
+                        for (int m = 0; m < mats; m++) {
+                            uint32_t r[16];
+                            q4k_half_cols(raw + m * kSbBytes + ct * 144, c + h, nib, r);
+                            tmem_st16(a_lanes + (uint32_t)((ab * 2 + m) * 32), r);
+                        }
                     }
                     tmem_wait_st();
                     tc_fence_before();
                     __syncwarp();
-                    if (lane == 0) arrive(&bars.a_full[ab]);
+                    if (lane == 0)
+                        for (int h = 0; h < kGrp; h++) arrive(&bars.a_full[(gch + h) % kAStages]);
                 }
                 __syncwarp();
                 if (lane == 0) arrive(&bars.raw_empty[st]);
