@@ -65,12 +65,12 @@ constexpr int kSbBytes = kTcRows * 144;           // one superblock of 128 Q4_K 
 constexpr int kRawStage = 2 * kSbBytes;           // gate + up
 constexpr int kRawStages = 3;
 constexpr int kOffRaw = 0;
-constexpr int kBStages = 4;
 constexpr int kScRows = 2 * kTcRows * 16;         // d, dmin, m[8] per row per matrix
 // Layout of one instantiation for token tiles of up to TOK tokens.
 template <int TOK>
 struct Cfg {
     static constexpr int kBBytes = 2 * TOK * 128;             // B: TOK hi rows, then TOK lo rows, 128 B each
+    static constexpr int kBStages = TOK <= 32 ? 8 : 4;        // B ring depth (covers L2 latency)
     static constexpr int kScXs = 8 * TOK * 4;                 // the superblock's 8 group sums per row [row][8]
     static constexpr int kScSlot = kScRows + kScXs + 4 * TOK * 4;  // + scales [row][4]
     static constexpr int kVBytes = TOK * kTcRows * 4;         // one tile's per-token outputs [token][row]
@@ -99,7 +99,7 @@ struct Bars {
     uint64_t item_full[4], item_empty[4], tab_full[4];
     uint64_t raw_full[kRawStages], raw_empty[kRawStages];
     uint64_t a_full[4], a_empty[4];
-    uint64_t b_full[kBStages], b_empty[kBStages];
+    uint64_t b_full[8], b_empty[8];
     uint64_t d_full[2], d_empty[2];
     uint64_t sc_full[4], sc_empty[4];
     uint64_t mma_done[2];
@@ -319,7 +319,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a,
     using C = Cfg<TOK>;
     constexpr int kTok = TOK, kBBytes = C::kBBytes, kScXs = C::kScXs, kScSlot = C::kScSlot, kOffB = C::kOffB,
                   kOffSc = C::kOffSc, kOffV = C::kOffV, kDCols = C::kDCols, kACol0 = C::kACol0,
-                  kAStages = C::kAStages;
+                  kAStages = C::kAStages, kBStages = C::kBStages;
     extern __shared__ __align__(1024) unsigned char smem[];
     __shared__ Bars bars;
     __shared__ Item items[4];
