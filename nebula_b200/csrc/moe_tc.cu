@@ -70,10 +70,10 @@ constexpr int kScRows = 2 * kTcRows * 16;         // d, dmin, m[8] per row per m
 template <int TOK>
 struct Cfg {
     static constexpr int kBBytes = 2 * TOK * 128;             // B: TOK hi rows, then TOK lo rows, 128 B each
-    static constexpr int kBStages = TOK <= 32 ? 8 : 4;        // B ring depth (covers L2 latency)
+    static constexpr int kBStages = TOK <= 32 ? 4 : 3;        // B ring depth
     static constexpr int kScXs = 8 * TOK * 4;                 // the superblock's 8 group sums per row [row][8]
     static constexpr int kScSlot = kScRows + kScXs + 4 * TOK * 4;  // + scales [row][4]
-    static constexpr int kVBytes = TOK * kTcRows * 4;         // one tile's per-token outputs [token][row]
+    static constexpr int kVBytes = 2 * TOK * kTcRows * 4;     // one tile's outputs [plane][slot][row] (gate/up: g, u)
     static constexpr int kOffB = kRawStages * kRawStage, kOffSc = kOffB + kBStages * kBBytes,
                          kOffV = kOffSc + 4 * kScSlot, kSmem = kOffV + kVBytes;
     // Tensor memory (512 columns): D[db][m] at (db*2+m)*kDCols, A[ab][m] (32
@@ -739,15 +739,15 @@ __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a,
 #pragma unroll
                     for (int pp = 0; pp < 4; pp++) {
                         if (cb * 8 + 2 * pp >= hw) break;  // the other half's slots
-                        float2 v = acc[0][cb * 4 + pp];
-                        if (gu) {
-                            const float2 u = acc[1][cb * 4 + pp];
-                            v.x = (v.x * sigmoidf_ref(v.x)) * u.x;
-                            v.y = (v.y * sigmoidf_ref(v.y)) * u.y;
-                        }
+                        const float2 v = acc[0][cb * 4 + pp];
                         const int j = j0 + cb * 8 + 2 * pp;
                         sv[j * kTcRows + r] = v.x;
                         sv[(j + 1) * kTcRows + r] = v.y;
+                        if (gu) {
+                            const float2 u = acc[1][cb * 4 + pp];
+                            sv[(kTok + j) * kTcRows + r] = u.x;
+                            sv[(kTok + j + 1) * kTcRows + r] = u.y;
+                        }
                     }
                 }
             }
@@ -758,8 +758,17 @@ __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a,
                 // scale from the tile's max |v|
 #pragma unroll 1
                 for (int j = ew; j < it.n; j += kEpiWarps) {
-                    const float *vj = sv + j * kTcRows;
-                    const float v0 = vj[lane], v1 = vj[32 + lane], v2 = vj[64 + lane], v3 = vj[96 + lane];
+                    // SwiGLU of the token's 128 rows, kept in plane 0 for the split below
+                    float *vj = sv + j * kTcRows;
+                    const float *uj = sv + (kTok + j) * kTcRows;
+                    float v[4];
+#pragma unroll
+                    for (int i = 0; i < 4; i++) {
+                        const float g = vj[32 * i + lane];
+                        v[i] = (g * sigmoidf_ref(g)) * uj[32 * i + lane];
+                        vj[32 * i + lane] = v[i];
+                    }
+                    const float v0 = v[0], v1 = v[1], v2 = v[2], v3 = v[3];
                     float s0 = v0, s1 = v1, s2 = v2, s3 = v3;
 #pragma unroll
                     for (int dd = 16; dd; dd >>= 1) {
