@@ -166,7 +166,9 @@ int qg_moe_layer(float *out, int *ids_out, float *weights_out, const float *x, i
  * The router is replicated, so every rank derives the same ids; each rank
  * computes its experts' weighted rows and stores them into every rank's
  * workspace over NVLink, then every rank reduces all rows in router-rank
- * order, so `out` on every rank is bitwise the single-GPU qg_moe_layer output.
+ * order. ids are bitwise those of qg_moe_layer; `out` matches it within the
+ * float tolerance of the path (gate/up tiles are split along K across SMs
+ * when each rank holds few experts, and the parts are added in fixed order).
  * workspaces[r] is rank r's workspace (qg_ep_workspace_bytes, zero-filled
  * once, allocated with qg_alloc) as seen from this process: this rank's own
  * pointer and the others mapped with qg_ep_ipc_open from the 64-byte handles

@@ -1138,8 +1138,9 @@ extern "C" int qg_moe_profile_read(int phase, double *total_ms, int *launches) {
 namespace {
 
 struct EpLayout {
-    size_t slots, shout, flags, epoch, total;
+    size_t slots, shout, flags, epoch, part, pcnt, total;
 };
+constexpr int kEpMaxSplit = 4;  // K parts of a gate/up tile under expert parallelism
 
 EpLayout ep_layout(int T, int H, int F) {
     EpLayout E{};
@@ -1153,6 +1154,8 @@ EpLayout ep_layout(int T, int H, int F) {
     E.shout = take(sizeof(float) * 2 * (size_t)T * H);         // [2][T][H]
     E.flags = take(sizeof(int) * kMaxRanks);                     // epoch reached by each source rank
     E.epoch = take(sizeof(int) * 2);                             // call epoch, combine ticket
+    E.part = take(sizeof(float) * ((size_t)T * kTop + T) * kEpMaxSplit * 2 * F);  // split-K partial sums
+    E.pcnt = take(sizeof(int) * (kExperts + 1) * (F / kTcRows));                 // parts finished per tile
     E.total = p;
     return E;
 }
@@ -1283,6 +1286,11 @@ extern "C" int qg_moe_layer_ep(float *out, int *ids_out, float *weights_out, con
         a.ep_flags[p] = reinterpret_cast<int *>(pb + EL.flags);
     }
     a.ep_epoch = reinterpret_cast<int *>(b + EL.epoch);
+    // fewer experts per rank: split each gate/up tile along K so every SM has work
+    a.gu_ks = ranks >= 4 ? 4 : ranks >= 2 ? 2 : 1;
+    while (a.gu_ks > 1 && (hidden / 256) % a.gu_ks) a.gu_ks >>= 1;
+    a.gu_part = reinterpret_cast<float *>(b + EL.part);
+    a.gu_pcnt = reinterpret_cast<int *>(b + EL.pcnt);
     int rc = dec_run_timed(a, st);
     if (rc) return rc;
     ep_combine_kernel<<<dim3((hidden + 255) / 256, tokens), 256, 0, st>>>(

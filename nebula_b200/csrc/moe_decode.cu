@@ -872,6 +872,7 @@ int dec_run(const DecArgs &in, cudaStream_t st, cudaEvent_t split) {
         t.gu_done = a.ctr->gu_done, t.tilecnt = a.ctr->tilecnt, t.err = &a.hdr->error;
         t.n_experts = a.n_experts;
         t.ep_ranks = a.ep_ranks, t.ep_rank = a.ep_rank, t.ep_epoch = a.ep_epoch;
+        t.gu_ks = a.gu_ks > 1 ? a.gu_ks : 1, t.gu_part = a.gu_part, t.gu_pcnt = a.gu_pcnt;
         for (int p = 0; p < kMaxRanks; p++)
             t.ep_slots[p] = a.ep_slots[p], t.ep_shout[p] = a.ep_shout[p], t.ep_flags[p] = a.ep_flags[p];
         TcMaps maps;

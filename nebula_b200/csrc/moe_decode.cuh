@@ -55,6 +55,9 @@ struct DecArgs {
     float *ep_slots[kMaxRanks], *ep_shout[kMaxRanks];
     int *ep_flags[kMaxRanks];
     int *ep_epoch;
+    int gu_ks;  // split K of gate/up tiles (1 = none)
+    float *gu_part;
+    int *gu_pcnt;
     // filled by dec_run
     int gstride, dn_rows, stage_bytes, k1_ctas;
 };

@@ -92,7 +92,7 @@ constexpr uint32_t kBad = 1u << 16;
 
 enum { kEnd = 0, kGU = 1, kDN = 2 };
 struct Item {
-    int kind, sub, mt, expert, first, n, tok0;
+    int kind, sub, mt, expert, first, n, tok0, kq;  // kq: K part of a gate/up tile
 };
 
 struct Bars {
@@ -328,10 +328,12 @@ __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a,
     __shared__ volatile int abort_flag;
     __shared__ int s_combine[kTok];
     __shared__ int s_ncombine;
+    __shared__ int s_last;  // this K part is the last of its gate/up tile
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int T = a.T, H = a.H, F = a.F;
     const int gu_mt = F / kTcRows, dn_mt = H / kTcRows;
-    const int gu_sb = H / 256, dn_sb = F / 256;
+    const int gu_ks = a.gu_ks > 1 ? a.gu_ks : 1;
+    const int gu_sb = H / 256 / gu_ks, dn_sb = F / 256;  // superblocks per item
     if (tid == 0) {
         for (int i = 0; i < 4; i++) {
             mbar_init(&bars.item_full[i], 1);
@@ -377,7 +379,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a,
         if (lane == 0) {
             bool planned = false;
             int nsub = a.shared_subs, gsb = 0;
-            const int S_gu = a.shared_subs * gu_mt;
+            const int S_gu = a.shared_subs * gu_mt * gu_ks;
             for (int seq = 0;; seq++) {
                 const int slot = seq & 3;
                 int idx = 1 << 30;
@@ -388,10 +390,10 @@ __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a,
                     nsub = __ldcg(a.n_sub);
                     planned = true;
                 }
-                Item it{kEnd, 0, 0, -1, 0, 0, 0};
-                const int total_gu = nsub * gu_mt, total_dn = nsub * dn_mt;
+                Item it{kEnd, 0, 0, -1, 0, 0, 0, 0};
+                const int total_gu = nsub * gu_mt * gu_ks, total_dn = nsub * dn_mt;
                 if (idx < total_gu) {
-                    it.kind = kGU, it.sub = idx / gu_mt, it.mt = idx % gu_mt;
+                    it.kind = kGU, it.sub = idx / (gu_mt * gu_ks), it.mt = (idx / gu_ks) % gu_mt, it.kq = idx % gu_ks;
                 } else if (idx < total_gu + total_dn) {
                     it.kind = kDN, it.sub = (idx - total_gu) / dn_mt, it.mt = (idx - total_gu) % dn_mt;
                 }
@@ -417,8 +419,9 @@ __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a,
                     if (it.kind == kGU) {
                         const int y = (it.expert < 0 ? 0 : it.expert * F) + it.mt * kTcRows;
                         mbar_arrive_expect_tx(&bars.raw_full[st], 2 * kSbBytes);
-                        tma_2d(dst, it.expert < 0 ? &maps.sg : &maps.gate, sb * 144, y, &bars.raw_full[st]);
-                        tma_2d(dst + kSbBytes, it.expert < 0 ? &maps.su : &maps.up, sb * 144, y, &bars.raw_full[st]);
+                        const int x = (it.kq * gu_sb + sb) * 144;
+                        tma_2d(dst, it.expert < 0 ? &maps.sg : &maps.gate, x, y, &bars.raw_full[st]);
+                        tma_2d(dst + kSbBytes, it.expert < 0 ? &maps.su : &maps.up, x, y, &bars.raw_full[st]);
                     } else {
                         const int y = (it.expert < 0 ? 0 : it.expert * H) + it.mt * kTcRows;
                         mbar_arrive_expect_tx(&bars.raw_full[st], kSbBytes);
@@ -523,7 +526,8 @@ __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a,
                         break;
                     unsigned char *scb = smem + kOffSc + sc_slot * kScSlot;
                     mbar_arrive_expect_tx(&bars.sc_full[sc_slot], kScXs + 4 * kTok * 4);
-                    tma_2d(scb + kScRows, gs, sb * 8, brow, &bars.sc_full[sc_slot]);
+                    const int gsbk = gu ? it.kq * gu_sb + sb : sb;  // superblock index along K
+                    tma_2d(scb + kScRows, gs, gsbk * 8, brow, &bars.sc_full[sc_slot]);
                     tma_2d(scb + kScRows + kScXs, iv, gu ? 0 : (2 * sb) & ~3, brow, &bars.sc_full[sc_slot]);
                     for (int c = 0; c < 4; c++, gch++) {
                         const int bs = gch % kBStages;
@@ -532,8 +536,8 @@ __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a,
                             break;
                         unsigned char *bt = smem + kOffB + bs * kBBytes;
                         mbar_arrive_expect_tx(&bars.b_full[bs], kBBytes);
-                        tma_2d(bt, bh, (sb * 4 + c) * 64, brow, &bars.b_full[bs]);
-                        tma_2d(bt + kTok * 128, bl, (sb * 4 + c) * 64, brow, &bars.b_full[bs]);
+                        tma_2d(bt, bh, (gsbk * 4 + c) * 64, brow, &bars.b_full[bs]);
+                        tma_2d(bt + kTok * 128, bl, (gsbk * 4 + c) * 64, brow, &bars.b_full[bs]);
                     }
                 }
                 arrive(&bars.item_empty[slot]);
@@ -753,7 +757,46 @@ __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a,
             }
             bar_named(3, 256);
             const int rr = et & 127;  // row handled by this thread in the per-token loops
-            if (gu) {
+            bool finish = true;
+            if (gu && gu_ks > 1) {
+                // this K part's partial sums; the last part of the tile adds them up in
+                // part order and finishes it
+                const size_t F2 = 2 * (size_t)F;
+#pragma unroll 1
+                for (int j = et >> 7; j < it.n; j += 2) {
+                    float *pp = a.gu_part + ((size_t)tb.mrow[j] * gu_ks + it.kq) * F2 + it.mt * kTcRows + rr;
+                    pp[0] = sv[j * kTcRows + rr];
+                    pp[F] = sv[(kTok + j) * kTcRows + rr];
+                }
+                __threadfence();
+                bar_named(3, 256);
+                if (et == 0) {
+                    int *cnt = a.gu_pcnt + it.sub * gu_mt + it.mt;
+                    const int last = atomicAdd(cnt, 1) == gu_ks - 1;
+                    if (last) *cnt = 0;
+                    s_last = last;
+                }
+                bar_named(3, 256);
+                finish = s_last != 0;
+                if (finish) {
+                    __threadfence();
+#pragma unroll 1
+                    for (int j = et >> 7; j < it.n; j += 2) {
+                        const float *pp = a.gu_part + (size_t)tb.mrow[j] * gu_ks * F2 + it.mt * kTcRows + rr;
+                        float g = 0.0f, u = 0.0f;
+                        for (int q = 0; q < gu_ks; q++) {
+                            g += __ldcg(pp + q * F2);
+                            u += __ldcg(pp + q * F2 + F);
+                        }
+                        sv[j * kTcRows + rr] = g;
+                        sv[(kTok + j) * kTcRows + rr] = u;
+                    }
+                }
+                bar_named(3, 256);
+            }
+            if (gu && !finish) {
+                // another K part finishes this tile
+            } else if (gu) {
                 // per token (one warp each): the four 32-row group sums and a power-of-two
                 // scale from the tile's max |v|
 #pragma unroll 1

@@ -53,6 +53,13 @@ struct TcArgs {
     // parity of the call epoch) instead of combining, and the last CTA raises
     // this rank's flag in every rank; a separate combine kernel reduces.
     int ep_ranks, ep_rank;
+    // Split K of gate/up tiles (gu_ks parts of gate/up superblocks, 1 = none):
+    // each part writes fp32 partial sums [row][part][gate|up][F] into gu_part,
+    // and the last part of a (sub-job, row tile) - counted in gu_pcnt, zero
+    // between calls - sums them in part order and finishes the tile.
+    int gu_ks;
+    float *gu_part;
+    int *gu_pcnt;
     float *ep_slots[kMaxRanks];   // per rank: [2][T*10][H]
     float *ep_shout[kMaxRanks];   // per rank: [2][T][H]
     int *ep_flags[kMaxRanks];     // per rank: [kMaxRanks] epoch reached by each source rank
