@@ -101,7 +101,7 @@ int qg_mtp_moe(float *slots, float *mid, const float *x, const int *ids, const f
  * ===================================================================== */
 
 /* Device workspace, in bytes, that qg_moe_routed / qg_moe_layer need for a
- * batch of `tokens` at the given shape. Replaces the per-layer host read of
+ * batch of up to `tokens` at the given shape. Replaces the per-layer host read of
  * route ids (qwen/qwen.c:649) and the per-expert launch loop
  * (qwen/qwen.c:680-698) with device-side grouping. Fill a new workspace with
  * zeros once (qg_zero): its counters start at zero and every call returns
@@ -128,7 +128,7 @@ int qg_moe_routed(float *out, const float *x, const int *ids, const float *weigh
 /* qg_moe_routed without a caller workspace (no counterpart in the reference):
  * for callers that cannot allocate device memory where they call, e.g. a
  * runtime whose device memory another allocator reserves in full up front.
- * The library keeps one static 4 MiB scratch per device (a T <= 17 batch at
+ * The library keeps one static 8 MiB scratch per device (a T <= 17 batch at
  * hidden 2048 / ffn 512 fits); shapes whose qg_moe_workspace_bytes exceed it
  * return cudaErrorInvalidValue before anything is launched. Nothing is
  * allocated. The first call on a device looks the scratch up and zeroes it

@@ -966,8 +966,9 @@ int run_experts(float *out, const float *x, const int *ids, const float *wts, in
 
 extern "C" int qg_moe_workspace_bytes(int tokens, int hidden, int ffn, size_t *bytes) {
     if (!bytes || check_shape(tokens, hidden, ffn)) return cudaErrorInvalidValue;
+    // every smaller batch fits too (both layouts grow with the token count)
     size_t n = layout(tokens, hidden, ffn).total;
-    if (tokens <= kMaxDecodeTokens) n = std::max(n, dec_layout(tokens, hidden, ffn).total);
+    n = std::max(n, dec_layout(std::min(tokens, kMaxDecodeTokens), hidden, ffn).total);
     *bytes = n;
     return 0;
 }
@@ -1005,6 +1006,7 @@ DecArgs dec_args(int T, int H, int F, int gt, int dt, const float *x, float *out
     a.n_sub = reinterpret_cast<int *>(b + L.nsub);
     a.mid16 = reinterpret_cast<__half *>(b + L.mid16);
     a.midinv = reinterpret_cast<float *>(b + L.midinv);
+    a.gu_part = reinterpret_cast<float *>(b + L.part);
     a.n_experts = kExperts;
     a.ep_shared_here = 1;
     return a;
@@ -1138,9 +1140,8 @@ extern "C" int qg_moe_profile_read(int phase, double *total_ms, int *launches) {
 namespace {
 
 struct EpLayout {
-    size_t slots, shout, flags, epoch, part, pcnt, total;
+    size_t slots, shout, flags, epoch, total;
 };
-constexpr int kEpMaxSplit = 4;  // K parts of a gate/up tile under expert parallelism
 
 EpLayout ep_layout(int T, int H, int F) {
     EpLayout E{};
@@ -1154,8 +1155,6 @@ EpLayout ep_layout(int T, int H, int F) {
     E.shout = take(sizeof(float) * 2 * (size_t)T * H);         // [2][T][H]
     E.flags = take(sizeof(int) * kMaxRanks);                     // epoch reached by each source rank
     E.epoch = take(sizeof(int) * 2);                             // call epoch, combine ticket
-    E.part = take(sizeof(float) * ((size_t)T * kTop + T) * kEpMaxSplit * 2 * F);  // split-K partial sums
-    E.pcnt = take(sizeof(int) * (kExperts + 1) * (F / kTcRows));                 // parts finished per tile
     E.total = p;
     return E;
 }
@@ -1286,11 +1285,6 @@ extern "C" int qg_moe_layer_ep(float *out, int *ids_out, float *weights_out, con
         a.ep_flags[p] = reinterpret_cast<int *>(pb + EL.flags);
     }
     a.ep_epoch = reinterpret_cast<int *>(b + EL.epoch);
-    // fewer experts per rank: split each gate/up tile along K so every SM has work
-    a.gu_ks = ranks >= 4 ? 4 : ranks >= 2 ? 2 : 1;
-    while (a.gu_ks > 1 && (hidden / 256) % a.gu_ks) a.gu_ks >>= 1;
-    a.gu_part = reinterpret_cast<float *>(b + EL.part);
-    a.gu_pcnt = reinterpret_cast<int *>(b + EL.pcnt);
     int rc = dec_run_timed(a, st);
     if (rc) return rc;
     ep_combine_kernel<<<dim3((hidden + 255) / 256, tokens), 256, 0, st>>>(

@@ -809,6 +809,7 @@ DecLayout dec_layout(int T, int H, int F) {
     L.nsub = take(sizeof(int));
     L.mid16 = take(sizeof(__half) * (T * kTop + T) * 2 * F);
     L.midinv = take(sizeof(float) * (T * kTop + T) * (((F / 128) + 3) & ~3));
+    L.part = take(sizeof(float) * (T * kTop + T) * kMaxParts * 2 * F);  // gate/up K-part sums
     L.total = p;
     return L;
 }
@@ -872,7 +873,7 @@ int dec_run(const DecArgs &in, cudaStream_t st, cudaEvent_t split) {
         t.gu_done = a.ctr->gu_done, t.tilecnt = a.ctr->tilecnt, t.err = &a.hdr->error;
         t.n_experts = a.n_experts;
         t.ep_ranks = a.ep_ranks, t.ep_rank = a.ep_rank, t.ep_epoch = a.ep_epoch;
-        t.gu_ks = a.gu_ks > 1 ? a.gu_ks : 1, t.gu_part = a.gu_part, t.gu_pcnt = a.gu_pcnt;
+        if (a.F / kTcRows <= kMaxGuTiles) t.gu_part = a.gu_part, t.gu_pcnt = a.ctr->gu_pcnt;
         for (int p = 0; p < kMaxRanks; p++)
             t.ep_slots[p] = a.ep_slots[p], t.ep_shout[p] = a.ep_shout[p], t.ep_flags[p] = a.ep_flags[p];
         TcMaps maps;

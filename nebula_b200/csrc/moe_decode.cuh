@@ -7,6 +7,7 @@
 namespace nb {
 
 constexpr int kMaxDecodeTokens = 32;
+constexpr int kMaxGuTiles = 16;  // gate/up row tiles (ffn / 128) the balanced gate/up counters cover
 
 // Workspace prefix: status words, then counters that every call leaves at
 // zero for the next one. The general (large-batch) path never writes here.
@@ -17,13 +18,14 @@ struct DecCtr {
     int k1_ticket, queue, k2_ticket, tc_queue, tc_ticket, pad[11];
     int gu_done[kExperts + 1];
     int tilecnt[kMaxDecodeTokens * 64];
+    int gu_pcnt[(kExperts + 1) * kMaxGuTiles];  // K parts finished per gate/up tile
 };
 constexpr size_t kHdrBytes = 256;
 constexpr size_t kPrefixBytes = (kHdrBytes + sizeof(DecCtr) + 255) & ~size_t(255);
 
 struct DecLayout {
     size_t logits, sgate, ids, wts, xpair, xsum, off, used, pairs, expect, mid, msum, slots, shout;
-    size_t x16, xinv, sub, nsub, mid16, midinv, total;  // tensor-core path
+    size_t x16, xinv, sub, nsub, mid16, midinv, part, total;  // tensor-core path
 };
 DecLayout dec_layout(int T, int H, int F);
 
@@ -55,9 +57,7 @@ struct DecArgs {
     float *ep_slots[kMaxRanks], *ep_shout[kMaxRanks];
     int *ep_flags[kMaxRanks];
     int *ep_epoch;
-    int gu_ks;  // split K of gate/up tiles (1 = none)
-    float *gu_part;
-    int *gu_pcnt;
+    float *gu_part;  // balanced gate/up work: K-part sums (TcArgs; counters in DecCtr)
     // filled by dec_run
     int gstride, dn_rows, stage_bytes, k1_ctas;
 };

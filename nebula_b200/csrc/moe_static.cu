@@ -21,8 +21,8 @@
 namespace {
 
 // Largest workspace this entry point serves: a T <= 17 verify batch at hidden
-// 2048 / FFN 512 needs 3.8 MiB (qg_moe_workspace_bytes).
-constexpr size_t kStaticScratchBytes = size_t(4) << 20;
+// 2048 / FFN 512 needs 4.7 MiB (qg_moe_workspace_bytes), T <= 28 fits.
+constexpr size_t kStaticScratchBytes = size_t(8) << 20;
 constexpr int kMaxDevices = 64;
 
 __device__ __align__(256) unsigned char g_moe_scratch[kStaticScratchBytes];

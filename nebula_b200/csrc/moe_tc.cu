@@ -91,8 +91,10 @@ static_assert(kTokDecode <= kTcTok, "tile sizes");
 constexpr uint32_t kBad = 1u << 16;
 
 enum { kEnd = 0, kGU = 1, kDN = 2 };
+// A gate/up item covers superblocks k0 .. k0+nk-1 of its tile, part kq of np
+// (np > 1: the tile is split along K between items; see the producer).
 struct Item {
-    int kind, sub, mt, expert, first, n, tok0, kq;  // kq: K part of a gate/up tile
+    int kind, sub, mt, expert, first, n, tok0, k0, nk, kq, np;
 };
 
 struct Bars {
@@ -332,8 +334,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a,
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int T = a.T, H = a.H, F = a.F;
     const int gu_mt = F / kTcRows, dn_mt = H / kTcRows;
-    const int gu_ks = a.gu_ks > 1 ? a.gu_ks : 1;
-    const int gu_sb = H / 256 / gu_ks, dn_sb = F / 256;  // superblocks per item
+    const int nsbk = H / 256, dn_sb = F / 256;  // superblocks of a whole gate/up tile, of a down tile
     if (tid == 0) {
         for (int i = 0; i < 4; i++) {
             mbar_init(&bars.item_full[i], 1);
@@ -377,25 +378,52 @@ __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a,
         // ------------------------------------------------------ producer
         regs_dec();
         if (lane == 0) {
+            // Claim order: the shared expert's gate/up tiles (whole; known before the
+            // routing), then the routed gate/up superblocks in ranges of q, then the
+            // down tiles. With gu_part, q spreads the routed tiles' superblocks
+            // evenly over the CTAs left (q >= half a tile keeps a tile in at most
+            // kMaxParts ranges); a range that crosses tile boundaries becomes one
+            // item per tile piece, and pieces of one tile are summed in part order.
             bool planned = false;
             int nsub = a.shared_subs, gsb = 0;
-            const int S_gu = a.shared_subs * gu_mt * gu_ks;
+            const int S_gu = a.shared_subs * gu_mt;
+            int q = nsbk, n_rng = 0, U = 0;  // routed range length, ranges, superblocks
+            int r_beg = 0, r_end = 0, r_id = 0;  // the claimed range's superblocks not yet emitted
             for (int seq = 0;; seq++) {
                 const int slot = seq & 3;
-                int idx = 1 << 30;
                 const bool ok = seq < 4 || wait_phase(&bars.item_empty[slot], ((seq >> 2) - 1) & 1, &abort_flag, err);
-                if (ok && !abort_flag) idx = atomicAdd(a.queue, 1);
-                if (idx >= S_gu && idx != (1 << 30) && !planned) {
-                    grid_dep_wait();  // routed work: the plan comes from the preceding kernel
-                    nsub = __ldcg(a.n_sub);
-                    planned = true;
-                }
-                Item it{kEnd, 0, 0, -1, 0, 0, 0, 0};
-                const int total_gu = nsub * gu_mt * gu_ks, total_dn = nsub * dn_mt;
-                if (idx < total_gu) {
-                    it.kind = kGU, it.sub = idx / (gu_mt * gu_ks), it.mt = (idx / gu_ks) % gu_mt, it.kq = idx % gu_ks;
-                } else if (idx < total_gu + total_dn) {
-                    it.kind = kDN, it.sub = (idx - total_gu) / dn_mt, it.mt = (idx - total_gu) % dn_mt;
+                Item it{kEnd, 0, 0, -1, 0, 0, 0, 0, 0, 0, 1};
+                if (ok && !abort_flag) {
+                    if (r_beg >= r_end) {
+                        const int idx = atomicAdd(a.queue, 1);
+                        if (idx >= S_gu && !planned) {
+                            grid_dep_wait();  // routed work: the plan comes from the preceding kernel
+                            nsub = __ldcg(a.n_sub);
+                            planned = true;
+                            U = (nsub - a.shared_subs) * gu_mt * nsbk;
+                            if (a.gu_part && U > 0) {
+                                const int g2 = max(1, (int)gridDim.x - S_gu);
+                                q = max((nsbk + 1) / 2, (U + g2 - 1) / g2);
+                            }
+                            n_rng = (U + q - 1) / q;
+                        }
+                        const int total_dn = nsub * dn_mt;
+                        if (idx < S_gu) {
+                            it.kind = kGU, it.sub = idx / gu_mt, it.mt = idx % gu_mt, it.nk = nsbk;
+                        } else if (idx < S_gu + n_rng) {
+                            r_id = idx - S_gu, r_beg = r_id * q, r_end = min(U, r_beg + q);
+                        } else if (idx < S_gu + n_rng + total_dn) {
+                            const int d = idx - S_gu - n_rng;
+                            it.kind = kDN, it.sub = d / dn_mt, it.mt = d % dn_mt;
+                        }
+                    }
+                    if (r_beg < r_end) {  // the range's piece within its next tile
+                        const int tile = r_beg / nsbk, k0 = r_beg % nsbk, nk = min(nsbk - k0, r_end - r_beg);
+                        const int f = tile * nsbk / q, l = ((tile + 1) * nsbk - 1) / q;
+                        it.kind = kGU, it.sub = a.shared_subs + tile / gu_mt, it.mt = tile % gu_mt;
+                        it.k0 = k0, it.nk = nk, it.kq = r_id - f, it.np = l - f + 1;
+                        r_beg += nk;
+                    }
                 }
                 if (it.kind != kEnd) {
                     if (it.sub < a.shared_subs) {  // known without the routing
@@ -409,7 +437,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a,
                 items[slot] = it;
                 arrive(&bars.item_full[slot]);
                 if (it.kind == kEnd) break;
-                const int nsb = it.kind == kGU ? gu_sb : dn_sb;
+                const int nsb = it.kind == kGU ? it.nk : dn_sb;
                 for (int sb = 0; sb < nsb; sb++, gsb++) {
                     const int st = gsb % kRawStages;
                     if (gsb >= kRawStages &&
@@ -419,7 +447,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a,
                     if (it.kind == kGU) {
                         const int y = (it.expert < 0 ? 0 : it.expert * F) + it.mt * kTcRows;
                         mbar_arrive_expect_tx(&bars.raw_full[st], 2 * kSbBytes);
-                        const int x = (it.kq * gu_sb + sb) * 144;
+                        const int x = (it.k0 + sb) * 144;
                         tma_2d(dst, it.expert < 0 ? &maps.sg : &maps.gate, x, y, &bars.raw_full[st]);
                         tma_2d(dst + kSbBytes, it.expert < 0 ? &maps.su : &maps.up, x, y, &bars.raw_full[st]);
                     } else {
@@ -449,7 +477,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a,
                 const Item it = items[slot];
                 if (it.kind == kEnd) break;
                 const bool gu = it.kind == kGU;
-                const int nsb = gu ? gu_sb : dn_sb;
+                const int nsb = gu ? it.nk : dn_sb;
                 bool ok = true;
                 for (int sb = 0; sb < nsb && ok; sb++, gsb++) {
                     const int db = gsb & 1;
@@ -519,14 +547,14 @@ __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a,
                 const int brow = (gu && a.all_tok) ? 0 : row0;
                 const CUtensorMap *bh = gu ? &maps.bx_hi : &maps.bm_hi, *bl = gu ? &maps.bx_lo : &maps.bm_lo;
                 const CUtensorMap *gs = gu ? &maps.sx : &maps.sm, *iv = gu ? &maps.ix : &maps.im;
-                const int nsb = gu ? gu_sb : dn_sb;
+                const int nsb = gu ? it.nk : dn_sb;
                 for (int sb = 0; sb < nsb && ok; sb++, gsb++) {
                     const int sc_slot = gsb & 3;
                     if (gsb >= 4 && !(ok = wait_phase(&bars.sc_empty[sc_slot], ((gsb >> 2) - 1) & 1, &abort_flag, err)))
                         break;
                     unsigned char *scb = smem + kOffSc + sc_slot * kScSlot;
                     mbar_arrive_expect_tx(&bars.sc_full[sc_slot], kScXs + 4 * kTok * 4);
-                    const int gsbk = gu ? it.kq * gu_sb + sb : sb;  // superblock index along K
+                    const int gsbk = gu ? it.k0 + sb : sb;  // superblock index along K
                     tma_2d(scb + kScRows, gs, gsbk * 8, brow, &bars.sc_full[sc_slot]);
                     tma_2d(scb + kScRows + kScXs, iv, gu ? 0 : (2 * sb) & ~3, brow, &bars.sc_full[sc_slot]);
                     for (int c = 0; c < 4; c++, gch++) {
@@ -560,7 +588,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a,
             const Item it = items[slot];
             if (it.kind == kEnd) break;
             const int mats = it.kind == kGU ? 2 : 1;
-            const int nsb = it.kind == kGU ? gu_sb : dn_sb;
+            const int nsb = it.kind == kGU ? it.nk : dn_sb;
             bool ok = true;
             for (int sb = 0; sb < nsb && ok; sb++, gsb++) {
                 const int st = gsb % kRawStages, sc_slot = gsb & 3;
@@ -634,7 +662,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a,
             // multiplied all T tokens
             const int hw = ((it.n + 3) >> 2) << 1;
             const int j0 = half * hw;
-            const int nsb = gu ? gu_sb : dn_sb;
+            const int nsb = gu ? it.nk : dn_sb;
             float2 acc[2][kHalf / 2];
 #pragma unroll
             for (int m = 0; m < 2; m++)
@@ -758,13 +786,13 @@ __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a,
             bar_named(3, 256);
             const int rr = et & 127;  // row handled by this thread in the per-token loops
             bool finish = true;
-            if (gu && gu_ks > 1) {
+            if (gu && it.np > 1) {
                 // this K part's partial sums; the last part of the tile adds them up in
                 // part order and finishes it
                 const size_t F2 = 2 * (size_t)F;
 #pragma unroll 1
                 for (int j = et >> 7; j < it.n; j += 2) {
-                    float *pp = a.gu_part + ((size_t)tb.mrow[j] * gu_ks + it.kq) * F2 + it.mt * kTcRows + rr;
+                    float *pp = a.gu_part + ((size_t)tb.mrow[j] * kMaxParts + it.kq) * F2 + it.mt * kTcRows + rr;
                     pp[0] = sv[j * kTcRows + rr];
                     pp[F] = sv[(kTok + j) * kTcRows + rr];
                 }
@@ -772,7 +800,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a,
                 bar_named(3, 256);
                 if (et == 0) {
                     int *cnt = a.gu_pcnt + it.sub * gu_mt + it.mt;
-                    const int last = atomicAdd(cnt, 1) == gu_ks - 1;
+                    const int last = atomicAdd(cnt, 1) == it.np - 1;
                     if (last) *cnt = 0;
                     s_last = last;
                 }
@@ -782,9 +810,9 @@ __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a,
                     __threadfence();
 #pragma unroll 1
                     for (int j = et >> 7; j < it.n; j += 2) {
-                        const float *pp = a.gu_part + (size_t)tb.mrow[j] * gu_ks * F2 + it.mt * kTcRows + rr;
+                        const float *pp = a.gu_part + (size_t)tb.mrow[j] * kMaxParts * F2 + it.mt * kTcRows + rr;
                         float g = 0.0f, u = 0.0f;
-                        for (int q = 0; q < gu_ks; q++) {
+                        for (int q = 0; q < it.np; q++) {
                             g += __ldcg(pp + q * F2);
                             u += __ldcg(pp + q * F2 + F);
                         }

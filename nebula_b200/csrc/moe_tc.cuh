@@ -8,6 +8,7 @@ namespace nb {
 constexpr int kTcTok = 48;     // tokens per sub-job (token tile of one expert)
 constexpr int kTcRows = 128;   // weight rows per tile (MMA M)
 constexpr int kMaxRanks = 8;   // expert-parallel ranks (GPUs of one box)
+constexpr int kMaxParts = 3;   // K parts of one gate/up tile (balanced gate/up work)
 
 // One token tile of one expert. expert < 0 is the shared expert, whose tokens
 // are tok0 .. tok0+n-1; a routed sub-job covers pairs[first .. first+n).
@@ -53,11 +54,12 @@ struct TcArgs {
     // parity of the call epoch) instead of combining, and the last CTA raises
     // this rank's flag in every rank; a separate combine kernel reduces.
     int ep_ranks, ep_rank;
-    // Split K of gate/up tiles (gu_ks parts of gate/up superblocks, 1 = none):
-    // each part writes fp32 partial sums [row][part][gate|up][F] into gu_part,
-    // and the last part of a (sub-job, row tile) - counted in gu_pcnt, zero
-    // between calls - sums them in part order and finishes the tile.
-    int gu_ks;
+    // Balanced gate/up work (gu_part non-null): the routed gate/up superblocks
+    // are dealt to the CTAs in equal contiguous ranges, so a tile may be split
+    // along K into up to kMaxParts items. Each writes fp32 partial sums
+    // [row][kMaxParts][gate|up][F] into gu_part, and the last to finish - counted
+    // in gu_pcnt[sub * F/128 + row tile], zero between calls - sums them in part
+    // order and finishes the tile. Null: whole tiles only.
     float *gu_part;
     int *gu_pcnt;
     float *ep_slots[kMaxRanks];   // per rank: [2][T*10][H]
