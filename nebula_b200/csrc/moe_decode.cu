@@ -6,11 +6,12 @@
 //     and computes logits in the reference's 32-lane order (bitwise equal to
 //     qc_matmul, so expert ids are bit-exact). CTA t < T also writes x[t] in
 //     the pair-interleaved layout the expert kernel reads, plus its 32-value
-//     group sums. The last CTA to finish (atomic ticket) runs top-10
-//     routing (qwen/gpu.cu:456-465 semantics) and builds the plan: per-expert
-//     token lists in ascending token order, offsets, the used-expert list and
+//     group sums. The last T CTAs to finish (atomic ticket) each run the
+//     top-10 routing of one token (qwen/gpu.cu:456-465 semantics) once all
+//     logits are in, and the last of them builds the plan: per-expert token
+//     lists in ascending token order, offsets, the used-expert list and
 //     per-token contribution counts. Without a router (qg_moe_routed) K1
-//     only stages x and plans from the given ids/weights.
+//     only stages x and the last CTA plans from the given ids/weights.
 //
 //  K2 dec_experts_kernel: persistent, one CTA per SM of eight warps. Thread 0
 //     also produces: it claims work items from a device queue and streams
@@ -180,9 +181,29 @@ __global__ void __launch_bounds__(kK1Threads) dec_router_kernel(DecArgs a) {
     }
     __threadfence();
     __syncthreads();
-    if (tid == 0) s_last = atomicAdd(&a.ctr->k1_ticket, 1) == (int)gridDim.x - 1;
+    const int G = gridDim.x;
+    __shared__ int s_tk;
+    if (tid == 0) s_tk = atomicAdd(&a.ctr->k1_ticket, 1);
     __syncthreads();
-    if (!s_last) return;
+    if (a.router) {
+        // The last T CTAs to finish route one token each, in parallel on their own
+        // SMs, once every CTA's logits are in (all K1 CTAs are resident, so the
+        // bounded wait only spans the last arrivals); the last of them plans.
+        const int t = s_tk - (G - T);
+        if (t < 0) return;
+        if (tid == 0) s_last = wait_geq(&a.ctr->k1_ticket, G, &a.hdr->error);
+        __syncthreads();
+        if (!s_last) return;
+        __threadfence();
+        if (warp == 0) route_token_warp(a.logits + t * kExperts, a.bias, a.ids + t * kTop, a.wts + t * kTop);
+        __threadfence();
+        __syncthreads();
+        if (tid == 0) s_last = atomicAdd(&a.ctr->k1_routed, 1) == T - 1;
+        __syncthreads();
+        if (!s_last) return;
+    } else if (s_tk != G - 1) {
+        return;
+    }
     __threadfence();
 
     // ---------------------------------------------------------- plan
@@ -192,12 +213,6 @@ __global__ void __launch_bounds__(kK1Threads) dec_router_kernel(DecArgs a) {
     __shared__ int s_off[kExperts];
     __shared__ int s_bad[kMaxDecodeTokens];
     __shared__ int s_wt[kK1Threads / 32], s_wu[kK1Threads / 32], s_wm[kK1Threads / 32], s_inv[kK1Threads / 32];
-    if (a.router) {
-        for (int t = warp; t < T; t += blockDim.x / 32)
-            route_token_warp(a.logits + t * kExperts, a.bias, a.ids + t * kTop, a.wts + t * kTop);
-        __threadfence();
-        __syncthreads();
-    }
     for (int i = tid; i < T * kTop; i += blockDim.x) {
         s_ids[i] = __ldcg(a.ids + i);
         s_w[i] = __ldcg(a.wts + i);
@@ -301,6 +316,7 @@ __global__ void __launch_bounds__(kK1Threads) dec_router_kernel(DecArgs a) {
         for (int w = 0; w < kK1Threads / 32; w++) inv += s_inv[w];
         a.hdr->invalid_tokens = inv;
         a.ctr->k1_ticket = 0;
+        a.ctr->k1_routed = 0;
     }
 }
 

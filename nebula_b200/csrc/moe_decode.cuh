@@ -15,7 +15,7 @@ struct DecHdr {
     int invalid_tokens, n_pairs, n_used, error;
 };
 struct DecCtr {
-    int k1_ticket, queue, k2_ticket, tc_queue, tc_ticket, pad[11];
+    int k1_ticket, queue, k2_ticket, tc_queue, tc_ticket, k1_routed, pad[10];
     int gu_done[kExperts + 1];
     int tilecnt[kMaxDecodeTokens * 64];
     int gu_pcnt[(kExperts + 1) * kMaxGuTiles];  // K parts finished per gate/up tile
