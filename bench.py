@@ -14,7 +14,9 @@ The stack's weights (43.5 GB) are far larger than L2 (126 MB), so every step
 streams its experts from HBM; no flush is needed.
 
 Extra keys: `prefill` (config 4: one layer, T=2048, N(0,1) logits fed to
-top-10), `roofline` (dominant kernel vs measured HBM copy bandwidth),
+top-10; one GPU), `prefill_ep` (config 5's prefill: one layer, T=2048 through
+the router with the Zipf bias and the shared expert; expert parallel at N>1,
+where rank r returns its 1/N of the tokens), `roofline` (dominant kernel vs measured HBM copy bandwidth),
 `cpu_baseline` (the reference's own CPU MoE on this host's cores), `e2e`
 (the same metric through the C ABI with pinned host buffers copied in and
 results read back every step).
@@ -388,6 +390,54 @@ def main() -> None:
         e2e_s = float(t.item())
     e2e_value = T * args.steps / e2e_s
 
+    # config 5's prefill: one layer at T=2048 with the router, Zipf bias and the
+    # shared expert (layer 0's weights), expert parallel at N>1; device time, max
+    # over ranks
+    prefill_ep = None
+    if not args.no_prefill:
+        P = 2048
+        d0 = stack.w[0]
+        dxp = L.synth_normal(P * H, 77)
+        outp = L.Device.empty((P, H), np.float32)
+        idp, wtp = L.Device.empty((P, K), np.int32), L.Device.empty((P, K), np.float32)
+        if ep_mode:
+            from nebula_b200 import ep as epm
+            pg = epm.EpGroup(P, H, F, rank, world)
+
+            def prep():
+                L.call("moe_layer_ep", outp.p, idp.p, wtp.p, dxp.p, P, d0["router"].p, d0["bias"].p, d0["gate"].p,
+                       Q4K, d0["up"].p, Q4K, d0["down"].p, Q4K, d0["n_local"], d0["local"].p, d0["sg"].p, Q4K,
+                       d0["su"].p, Q4K, d0["sd"].p, Q4K, d0["sr"].p, 0, H, F, rank, world, pg.ptrs)
+        else:
+            pws2 = L.workspace(P, H, F)
+
+            def prep():
+                L.call("moe_layer", outp.p, idp.p, wtp.p, dxp.p, P, d0["router"].p, d0["bias"].p, d0["gate"].p, Q4K,
+                       d0["up"].p, Q4K, d0["down"].p, Q4K, d0["sg"].p, Q4K, d0["su"].p, Q4K, d0["sd"].p, Q4K,
+                       d0["sr"].p, H, F, pws2.p)
+        for _ in range(3):
+            prep()
+        barrier()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        reps = max(3, args.steps // 4)
+        a.record()
+        for _ in range(reps):
+            prep()
+        b.record()
+        torch.cuda.synchronize()
+        pms = a.elapsed_time(b) / reps
+        if dist:
+            t = torch.tensor([pms], device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            pms = float(t.item())
+        prefill_ep = {"workload": "config 5 prefill: 1 layer, T=2048, router + Zipf bias + shared expert, "
+                                  f"{'expert parallel over %d GPUs (rank r returns its 1/%d of the tokens)' % (world, world) if ep_mode else 'one GPU'}",
+                      "tokens_per_s": P / (pms / 1e3), "ms_per_layer": pms}
+        if ep_mode:
+            barrier()
+            pg.close()
+            barrier()
+
     # prefill (config 4) on layer 0's weights
     prefill = None
     if not args.no_prefill and world == 1:  # config 4 is a single-GPU layer
@@ -460,6 +510,8 @@ def main() -> None:
     }
     if prefill:
         line["prefill"] = prefill
+    if prefill_ep:
+        line["prefill_ep"] = prefill_ep
     if cpu:
         line["cpu_baseline"] = cpu
     if rank == 0:

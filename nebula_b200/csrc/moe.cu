@@ -765,18 +765,24 @@ __global__ void combine_kernel(float *out, const float *slots, const int *ids, c
 // Turns the per-expert token lists into token tiles of at most 64 tokens
 // (shared expert first), per-token contribution counts (| bad bit), and
 // zeroes the counters the tensor-core kernel counts up.
+// Expert parallelism: ep_local (else null) maps each expert to its index on this
+// rank or -1, and the shared expert covers tokens [sh_t0, sh_t1) only; out is
+// null there (the combine kernel writes every row of the rank's tokens).
 __global__ void __launch_bounds__(1024) tc_plan_kernel(Plan pl, const int *ids, int T, int H, int has_shared,
                                                       SubJob *sub, int *n_sub, int *expect, int *gu_done,
-                                                      int *tilecnt, float *out) {
+                                                      int *tilecnt, float *out, const int *ep_local, int sh_t0,
+                                                      int sh_t1) {
     __shared__ int s_pre[kExperts];
     __shared__ int s_wt[32];
     __shared__ int s_total;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int S = has_shared ? (T + kTcTok - 1) / kTcTok : 0;
+    const int S = has_shared ? (sh_t1 - sh_t0 + kTcTok - 1) / kTcTok : 0;
     const int n_used = pl.hdr->n_used;
-    for (int i = tid; i < S; i += blockDim.x) sub[i] = SubJob{-1, 0, min(kTcTok, T - i * kTcTok), i * kTcTok};
+    for (int i = tid; i < S; i += blockDim.x)
+        sub[i] = SubJob{-1, 0, min(kTcTok, sh_t1 - sh_t0 - i * kTcTok), sh_t0 + i * kTcTok};
     int tiles = 0;
-    if (tid < kExperts && tid < n_used) tiles = (pl.counts[pl.used[tid]] + kTcTok - 1) / kTcTok;
+    if (tid < kExperts && tid < n_used && (!ep_local || __ldg(ep_local + pl.used[tid]) >= 0))
+        tiles = (pl.counts[pl.used[tid]] + kTcTok - 1) / kTcTok;
     int incl = tiles;
 #pragma unroll
     for (int d = 1; d < 32; d <<= 1) {
@@ -800,8 +806,9 @@ __global__ void __launch_bounds__(1024) tc_plan_kernel(Plan pl, const int *ids, 
     __syncthreads();
     if (tid < kExperts && tid < n_used) {
         const int e = pl.used[tid], n = pl.counts[e], first = pl.off[e];
+        const int loc = ep_local ? __ldg(ep_local + e) : e;
         for (int i = 0; i < tiles; i++)
-            sub[S + s_pre[tid] + i] = SubJob{e, first + i * kTcTok, min(kTcTok, n - i * kTcTok), 0};
+            sub[S + s_pre[tid] + i] = SubJob{loc, first + i * kTcTok, min(kTcTok, n - i * kTcTok), 0};
     }
     const int total = S + s_total;
     if (tid == 0) *n_sub = total;
@@ -815,7 +822,7 @@ __global__ void __launch_bounds__(1024) tc_plan_kernel(Plan pl, const int *ids, 
             for (int k = 0; k < kTop; k++) n += ids[t * kTop + k] >= 0;
         const int e = n + has_shared;
         expect[t] = e | (bad ? 0x10000 : 0);
-        if (e == 0) {
+        if (e == 0 && out) {
             const float v = bad ? __int_as_float(0x7fc00000) : 0.0f;
             for (int d = 0; d < H; d++) out[(size_t)t * H + d] = v;
         }
@@ -859,10 +866,20 @@ int launch_down(const DownArgs &a, cudaStream_t st) {
 }
 
 // Routed experts (+ optional shared expert) from device ids/weights.
+// Expert parallelism over a large batch (run_experts): this rank's experts and
+// token block [t0, t1) (tokens of rank r: r*block ..), and the ranks' buffers.
+struct EpRun {
+    const int *local;  // [512] each expert's index on this rank, or -1
+    int n_local, ranks, rank, block, t0, t1;
+    float *slots[kMaxRanks], *shout[kMaxRanks];
+    int *flags[kMaxRanks];
+    int *epoch;
+};
+
 int run_experts(float *out, const float *x, const int *ids, const float *wts, int T, const void *gate, int gt,
                 const void *up, int ut, const void *down, int dt, const void *sg, int sgt, const void *su, int sut,
                 const void *sd, int sdt, const float *sgate, int sgate_stride, int H, int F, void *ws,
-                cudaStream_t st) {
+                cudaStream_t st, const EpRun *ep = nullptr) {
     if (int rc = check_shape(T, H, F)) return rc;
     if (!out || !x || !ids || !wts || !gate || !up || !down || !ws) return cudaErrorInvalidValue;
     if (gt != ut || (gt != 12 && gt != 20) || (dt != 12 && dt != 20)) return cudaErrorInvalidValue;
@@ -905,7 +922,8 @@ int run_experts(float *out, const float *x, const int *ids, const float *wts, in
         t.mi_stride = ((F / 128) + 3) & ~3;
         t.sub = reinterpret_cast<SubJob *>(base + L.sub);
         t.n_sub = reinterpret_cast<int *>(base + L.nsub);
-        t.shared_subs = has_shared ? (T + kTcTok - 1) / kTcTok : 0;
+        t.sh_t0 = ep ? ep->t0 : 0, t.sh_t1 = ep ? ep->t1 : T;
+        t.shared_subs = has_shared ? (t.sh_t1 - t.sh_t0 + kTcTok - 1) / kTcTok : 0;
         t.pairs = pl.pairs, t.wts = wts, t.ids = ids;
         t.expect = reinterpret_cast<int *>(base + L.expect);
         t.sgate = has_shared ? sgate : nullptr;
@@ -918,13 +936,20 @@ int run_experts(float *out, const float *x, const int *ids, const float *wts, in
         t.gu_done = reinterpret_cast<int *>(base + L.gudone);
         t.tilecnt = reinterpret_cast<int *>(base + L.tilecnt);
         t.err = &pl.hdr->error;
+        t.n_experts = ep ? ep->n_local : kExperts;
+        if (ep) {
+            t.ep_ranks = ep->ranks, t.ep_rank = ep->rank, t.ep_block = ep->block, t.ep_epoch = ep->epoch;
+            for (int r = 0; r < kMaxRanks; r++)
+                t.ep_slots[r] = ep->slots[r], t.ep_shout[r] = ep->shout[r], t.ep_flags[r] = ep->flags[r];
+        }
         TcMaps maps;
         if (int rc = tc_make_maps(t, maps, kTcTok)) return rc;
         {
             Span sp(kPlan, st);
             tc_plan_kernel<<<1, 1024, 0, st>>>(pl, ids, T, H, has_shared ? 1 : 0, const_cast<SubJob *>(t.sub),
                                                const_cast<int *>(t.n_sub), const_cast<int *>(t.expect), t.gu_done,
-                                               t.tilecnt, out);
+                                               t.tilecnt, ep ? nullptr : out, ep ? ep->local : nullptr, t.sh_t0,
+                                               t.sh_t1);
             if (int rc = cudaGetLastError()) return rc;
             const int rc = t.all_tok ? tc_prep_launch(x, T, H, const_cast<__half *>(t.x16), const_cast<float *>(t.xinv),
                                                       const_cast<float *>(t.xsum), st)
@@ -1145,7 +1170,7 @@ struct EpLayout {
 
 EpLayout ep_layout(int T, int H, int F) {
     EpLayout E{};
-    size_t p = align256(dec_layout(T, H, F).total);
+    size_t p = align256(T <= kMaxDecodeTokens ? dec_layout(T, H, F).total : layout(T, H, F).total);
     auto take = [&](size_t bytes) {
         size_t at = p;
         p = align256(p + bytes);
@@ -1165,13 +1190,13 @@ __device__ __forceinline__ int ld_acquire_sys(const int *p) {
     return v;
 }
 
-// grid (H/256, T): out[t] = sum_k (rank order) slots[t][k] + sigmoid(g_t) * shared[t]
-// once every rank has raised its flag for this call.
+// grid (H/256, tokens from t0): out[t] = sum_k (rank order) slots[t][k] +
+// sigmoid(g_t) * shared[t] once every rank has raised its flag for this call.
 __global__ void ep_combine_kernel(float *out, const float *slots, const float *shout, const int *ids,
                                   const int *expect, const float *sgate, int has_shared, int T, int H, int ranks,
-                                  const int *flags, int *epoch, int *err) {
+                                  const int *flags, int *epoch, int *err, int t0) {
     __shared__ int s_ok;
-    const int t = blockIdx.y, d = blockIdx.x * blockDim.x + threadIdx.x;
+    const int t = t0 + blockIdx.y, d = blockIdx.x * blockDim.x + threadIdx.x;
     const int e = __ldcg(epoch);
     if (threadIdx.x == 0) {
         int ok = 1;
@@ -1215,7 +1240,7 @@ __global__ void ep_combine_kernel(float *out, const float *slots, const float *s
 }  // namespace
 
 extern "C" int qg_ep_workspace_bytes(int tokens, int hidden, int ffn, size_t *bytes) {
-    if (!bytes || check_shape(tokens, hidden, ffn) || tokens > kMaxDecodeTokens) return cudaErrorInvalidValue;
+    if (!bytes || check_shape(tokens, hidden, ffn)) return cudaErrorInvalidValue;
     *bytes = ep_layout(tokens, hidden, ffn).total;
     return 0;
 }
@@ -1248,8 +1273,9 @@ extern "C" int qg_moe_layer_ep(float *out, int *ids_out, float *weights_out, con
     if (ranks < 1 || ranks > kMaxRanks || rank < 0 || rank >= ranks || shared_rank < 0 || shared_rank >= ranks ||
         n_local < 1 || n_local > kExperts)
         return cudaErrorInvalidValue;
+    const bool large = tokens > kMaxDecodeTokens;
     if (gt != 12 || ut != 12 || dt != 12 || (sg && (sgt != 12 || sut != 12 || sdt != 12)) ||
-        !dec_supported(tokens, hidden, ffn, gt, dt) || !tc_supported(hidden, ffn, gt, dt))
+        (!large && !dec_supported(tokens, hidden, ffn, gt, dt)) || !tc_supported(hidden, ffn, gt, dt))
         return cudaErrorNotSupported;  // expert parallelism runs on the Q4_K tensor-core path
     void *workspace = workspaces[rank];
     for (int p = 0; p < ranks; p++)
@@ -1259,6 +1285,58 @@ extern "C" int qg_moe_layer_ep(float *out, int *ids_out, float *weights_out, con
                                       !aligned16(s_router))))
         return cudaErrorInvalidValue;
     cudaStream_t st = launch_stream;
+    if (large) {
+        // Large batch: every rank routes all tokens; rank r runs its experts on the
+        // pairs routed to them and the shared expert on its own tokens
+        // [r*block, (r+1)*block), stores each weighted row into the buffers of the
+        // token's rank, and combines its own tokens once every rank has finished.
+        const Layout L = layout(tokens, hidden, ffn);
+        const EpLayout EL = ep_layout(tokens, hidden, ffn);
+        char *b = static_cast<char *>(workspace);
+        float *logits = reinterpret_cast<float *>(b + L.logits);
+        float *sgate = logits + (size_t)tokens * kExperts;
+        int *ids = ids_out ? ids_out : reinterpret_cast<int *>(b + L.ids);
+        float *wts = weights_out ? weights_out : reinterpret_cast<float *>(b + L.wts);
+        int rc;
+        {
+            Span sp(kRouter, st);
+            rc = launch_matmul(logits, router, 0, kExperts, hidden, x, tokens, st);
+            if (!rc && sg) rc = launch_matmul(sgate, s_router, 0, 1, hidden, x, tokens, st);
+        }
+        if (rc) return rc;
+        {
+            Span sp(kRoute, st);
+            rc = launch_route(ids, wts, logits, logit_bias, tokens, st);
+        }
+        if (rc) return rc;
+        EpRun ep{};
+        ep.local = expert_local, ep.n_local = n_local, ep.ranks = ranks, ep.rank = rank;
+        ep.block = (tokens + ranks - 1) / ranks;
+        ep.t0 = std::min(tokens, rank * ep.block), ep.t1 = std::min(tokens, ep.t0 + ep.block);
+        for (int p = 0; p < ranks; p++) {
+            char *pb = static_cast<char *>(workspaces[p]);
+            ep.slots[p] = reinterpret_cast<float *>(pb + EL.slots);
+            ep.shout[p] = reinterpret_cast<float *>(pb + EL.shout);
+            ep.flags[p] = reinterpret_cast<int *>(pb + EL.flags);
+        }
+        ep.epoch = reinterpret_cast<int *>(b + EL.epoch);
+        if ((rc = run_experts(out, x, ids, wts, tokens, gate, gt, up, ut, down, dt, sg, sgt, su, sut, sd, sdt, sgate, 1,
+                              hidden, ffn, workspace, st, &ep)))
+            return rc;
+        if (ep.t1 > ep.t0) {
+            Span sp(kCombine, st);
+            ep_combine_kernel<<<dim3((hidden + 255) / 256, ep.t1 - ep.t0), 256, 0, st>>>(
+                out, ep.slots[rank], ep.shout[rank], ids, reinterpret_cast<const int *>(b + L.expect), sgate,
+                sg != nullptr, tokens, hidden, ranks, ep.flags[rank], ep.epoch,
+                &reinterpret_cast<Header *>(b + L.hdr)->error, ep.t0);
+        } else {  // no tokens here: still advance the call epoch after every rank's rows are in
+            ep_combine_kernel<<<dim3(1, 1), 32, 0, st>>>(out, ep.slots[rank], ep.shout[rank], ids,
+                                                         reinterpret_cast<const int *>(b + L.expect), sgate, 0, tokens,
+                                                         0, ranks, ep.flags[rank], ep.epoch,
+                                                         &reinterpret_cast<Header *>(b + L.hdr)->error, 0);
+        }
+        return cudaGetLastError();
+    }
     const DecLayout DL = dec_layout(tokens, hidden, ffn);
     const EpLayout EL = ep_layout(tokens, hidden, ffn);
     char *b = static_cast<char *>(workspace);
@@ -1290,6 +1368,6 @@ extern "C" int qg_moe_layer_ep(float *out, int *ids_out, float *weights_out, con
     ep_combine_kernel<<<dim3((hidden + 255) / 256, tokens), 256, 0, st>>>(
         out, reinterpret_cast<const float *>(b + EL.slots), reinterpret_cast<const float *>(b + EL.shout), ids,
         a.expect, a.sgate, sg != nullptr, tokens, hidden, ranks, reinterpret_cast<const int *>(b + EL.flags),
-        reinterpret_cast<int *>(b + EL.epoch), &a.hdr->error);
+        reinterpret_cast<int *>(b + EL.epoch), &a.hdr->error, 0);
     return cudaGetLastError();
 }

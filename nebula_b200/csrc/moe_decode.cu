@@ -882,6 +882,7 @@ int dec_run(const DecArgs &in, cudaStream_t st, cudaEvent_t split) {
         t.x16 = a.x16, t.xinv = a.xinv, t.xsum = a.xsum;
         t.mi_stride = ((a.F / 128) + 3) & ~3;
         t.sub = a.sub, t.n_sub = a.n_sub, t.shared_subs = (a.sg && a.ep_shared_here) ? 1 : 0;
+        t.sh_t0 = 0, t.sh_t1 = a.T;
         t.pairs = a.pairs, t.wts = a.wts, t.ids = a.ids, t.expect = a.expect, t.sgate = a.sg ? a.sgate : nullptr;
         t.mid16 = a.mid16, t.midinv = a.midinv, t.msum = a.msum;
         t.slots = a.slots, t.shout = a.shout, t.out = a.out;

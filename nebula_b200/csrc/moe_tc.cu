@@ -427,7 +427,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a,
                 }
                 if (it.kind != kEnd) {
                     if (it.sub < a.shared_subs) {  // known without the routing
-                        it.expert = -1, it.tok0 = it.sub * kTok, it.n = min(kTok, T - it.tok0), it.first = 0;
+                        it.expert = -1, it.tok0 = a.sh_t0 + it.sub * kTok, it.n = min(kTok, a.sh_t1 - it.tok0), it.first = 0;
                     } else {
                         it.expert = __ldcg(&a.sub[it.sub].expert);
                         it.first = __ldcg(&a.sub[it.sub].first);
@@ -883,7 +883,12 @@ __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a,
                         const size_t o = it.expert < 0 ? ((size_t)par * T + tb.tok[j]) * H + row
                                                        : ((size_t)par * T * kTop + tb.slot[j]) * H + row;
                         const float v = it.expert < 0 ? y : y * tb.w[j];
-                        for (int p = 0; p < a.ep_ranks; p++) (it.expert < 0 ? a.ep_shout[p] : a.ep_slots[p])[o] = v;
+                        if (a.ep_block > 0) {  // the token's owner only
+                            const int p = tb.tok[j] / a.ep_block;
+                            (it.expert < 0 ? a.ep_shout[p] : a.ep_slots[p])[o] = v;
+                        } else {
+                            for (int p = 0; p < a.ep_ranks; p++) (it.expert < 0 ? a.ep_shout[p] : a.ep_slots[p])[o] = v;
+                        }
                     }
                     __syncwarp();
                     if (lane == 0) arrive(&bars.item_empty[slot]);

@@ -54,6 +54,11 @@ struct TcArgs {
     // parity of the call epoch) instead of combining, and the last CTA raises
     // this rank's flag in every rank; a separate combine kernel reduces.
     int ep_ranks, ep_rank;
+    // ep_block > 0 (large batches): token t belongs to rank t / ep_block, and a
+    // down tile stores each row only into its owner's buffers.
+    int ep_block;
+    // The shared expert's tokens: [sh_t0, sh_t1), in sub-jobs of the tile size.
+    int sh_t0, sh_t1;
     // Balanced gate/up work (gu_part non-null): the routed gate/up superblocks
     // are dealt to the CTAs in equal contiguous ranges, so a tile may be split
     // along K into up to kMaxParts items. Each writes fp32 partial sums

@@ -3,8 +3,9 @@ qg_moe_layer_ep routing equals the single-GPU qg_moe_layer routing bit for bit
 and its output matches within the path's float tolerance (the gate/up tiles
 are split along K across SMs and their parts summed in fixed order), over
 three calls (both parities of the double-buffered slot rows), with the experts
-placed in snake order of a skewed ranking. Skipped on a machine with fewer
-than two GPUs."""
+placed in snake order of a skewed ranking. A verify batch (T=17) returns every
+token on every rank; a large batch (T=100) returns each rank's own block of
+tokens. Skipped on a machine with fewer than two GPUs."""
 import os
 import socket
 
@@ -14,7 +15,7 @@ import torch.multiprocessing as mp
 
 pytestmark = pytest.mark.gpu
 
-H, F, T = 2048, 512, 17
+H, F = 2048, 512
 QROW_H, QROW_F = H // 256 * 144, F // 256 * 144  # Q4_K row bytes
 
 
@@ -24,7 +25,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, results):
+def _worker(rank, world, port, results, T):
     import torch
     import torch.distributed as dist
     torch.cuda.set_device(rank)
@@ -66,6 +67,9 @@ def _worker(rank, world, port, results):
                    12, len(experts), dloc.p, sg.p, 12, su.p, 12, sd.p, 12, sr.p, call % world, H, F, rank, world,
                    grp.ptrs)
             a, b = ref.get().astype(np.float64), out.get().astype(np.float64)
+            if T > 32:  # this rank's tokens only
+                blk = (T + world - 1) // world
+                a, b = a[rank * blk:(rank + 1) * blk], b[rank * blk:(rank + 1) * blk]
             if not np.array_equal(rid.get(), eid.get()):
                 errors.append(f"call {call}: routing differs")
             r = float(np.linalg.norm(a - b) / np.linalg.norm(a))
@@ -84,12 +88,13 @@ def _worker(rank, world, port, results):
         dist.destroy_process_group()
 
 
-def test_expert_parallel_matches_single_gpu():
+@pytest.mark.parametrize("T", (17, 100))
+def test_expert_parallel_matches_single_gpu(T):
     import torch
     world = 2
     if torch.cuda.device_count() < world:
         pytest.skip("needs two GPUs")
     mgr = mp.get_context("spawn").Manager()
     results = mgr.dict()
-    mp.start_processes(_worker, args=(world, _free_port(), results), nprocs=world, start_method="spawn", join=True)
+    mp.start_processes(_worker, args=(world, _free_port(), results, T), nprocs=world, start_method="spawn", join=True)
     assert [results.get(r) for r in range(world)] == ["ok"] * world, dict(results)
