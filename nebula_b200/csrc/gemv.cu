@@ -1,9 +1,10 @@
 // Dense projections and element-wise operators of the qwen/gpu.h ABI:
 // qg_matmul, qg_gather, qg_dequant, qg_unary, qg_binary, qg_shared_add.
 //
-// qg_matmul keeps the reference's 32-lane accumulation order (one warp per
-// weight row, lane j owns columns j mod 32, then the 16/8/4/2/1 tree), so its
-// output is bitwise equal to qc_matmul (qwen/cpu.c:119-148). The router GEMV
+// qg_matmul keeps the reference's 32-lane accumulation order (lane j owns
+// columns j mod 32, then the 16/8/4/2/1 tree), so its output is bitwise equal
+// to qc_matmul (qwen/cpu.c:119-148): one warp per weight row, or for fp32 rows
+// against 64 or more tokens a tiled kernel with the same order per output. The router GEMV
 // that feeds top-10 selection relies on this for bit-exact expert ids.
 #include "quant.cuh"
 
@@ -39,6 +40,62 @@ __global__ void __launch_bounds__(kRowsPerCta * 32) matmul_kernel(float *out, co
             if ((threadIdx.x & 31) == 0) out[(size_t)(first + t) * rows + row] = s;
         }
     }
+}
+
+// fp32 weights, large batches: a CTA computes 16 rows x 32 tokens. Lane j of
+// every warp holds the partial sums over k = j (mod 32) of an 8-row x 8-token
+// tile, accumulated in increasing k with fused multiply-adds from 256-column
+// chunks of the rows and token vectors staged in shared memory, then the same
+// 16/8/4/2/1 tree: bitwise the order of one warp per row above.
+constexpr int kTR = 16, kTT = 32, kTK = 256, kTThreads = 256;
+__global__ void __launch_bounds__(kTThreads) matmul_f32_tiled_kernel(float *out, const float *w, int rows, int cols,
+                                                                     const float *x, int nt) {
+    __shared__ __align__(16) float ws[kTR][kTK];
+    __shared__ __align__(16) float xs[kTT][kTK];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int row0 = blockIdx.x * kTR, tok0 = blockIdx.y * kTT;
+    const int wr = (warp >> 2) * 8, wt = (warp & 3) * 8;  // this warp's rows and tokens within the tile
+    float acc[8][8];
+#pragma unroll
+    for (int r = 0; r < 8; r++)
+#pragma unroll
+        for (int t = 0; t < 8; t++) acc[r][t] = 0.0f;
+    for (int kc = 0; kc < cols; kc += kTK) {
+        const int kn = min(kTK, cols - kc);  // a multiple of 32
+        __syncthreads();
+        for (int i = tid; i < kTR * (kTK / 4); i += kTThreads) {
+            const int r = i / (kTK / 4), c = (i % (kTK / 4)) * 4;
+            float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            if (row0 + r < rows && c < kn) v = __ldg(reinterpret_cast<const float4 *>(w + (size_t)(row0 + r) * cols + kc + c));
+            *reinterpret_cast<float4 *>(&ws[r][c]) = v;
+        }
+        for (int i = tid; i < kTT * (kTK / 4); i += kTThreads) {
+            const int t = i / (kTK / 4), c = (i % (kTK / 4)) * 4;
+            float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            if (tok0 + t < nt && c < kn) v = __ldg(reinterpret_cast<const float4 *>(x + (size_t)(tok0 + t) * cols + kc + c));
+            *reinterpret_cast<float4 *>(&xs[t][c]) = v;
+        }
+        __syncthreads();
+        for (int k = lane; k < kn; k += 32) {
+            float wv[8], xv[8];
+#pragma unroll
+            for (int r = 0; r < 8; r++) wv[r] = ws[wr + r][k];
+#pragma unroll
+            for (int t = 0; t < 8; t++) xv[t] = xs[wt + t][k];
+#pragma unroll
+            for (int r = 0; r < 8; r++)
+#pragma unroll
+                for (int t = 0; t < 8; t++) acc[r][t] = __fmaf_rn(wv[r], xv[t], acc[r][t]);
+        }
+    }
+#pragma unroll
+    for (int r = 0; r < 8; r++)
+#pragma unroll
+        for (int t = 0; t < 8; t++) {
+            const float s = lane_tree(acc[r][t]);
+            const int row = row0 + wr + r, tok = tok0 + wt + t;
+            if (lane == 0 && row < rows && tok < nt) out[(size_t)tok * rows + row] = s;
+        }
 }
 
 __global__ void gather_kernel(float *out, const unsigned char *w, int type, int n, size_t stride, int row) {
@@ -82,6 +139,12 @@ int launch_matmul(float *o, const void *w, int type, int rows, int cols, const f
     size_t stride = row_bytes(type, cols);
     if (!o || !w || !x || !stride || rows < 1 || cols < 1 || nt < 1 || nt > kMaxTokens || !valid_cols(type, cols))
         return cudaErrorInvalidValue;
+    if (type == 0 && nt >= 64 && cols % 32 == 0 && !(reinterpret_cast<uintptr_t>(w) & 15) &&
+        !(reinterpret_cast<uintptr_t>(x) & 15)) {  // fp32 rows against a large batch: tiled
+        matmul_f32_tiled_kernel<<<dim3((rows + kTR - 1) / kTR, (nt + kTT - 1) / kTT), kTThreads, 0, st>>>(
+            o, static_cast<const float *>(w), rows, cols, x, nt);
+        return cudaGetLastError();
+    }
     dim3 grid((rows + kRowsPerCta - 1) / kRowsPerCta, (nt + kTokTile - 1) / kTokTile);
     const unsigned char *wb = static_cast<const unsigned char *>(w);
     switch (type) {

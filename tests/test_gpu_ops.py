@@ -64,13 +64,16 @@ def test_matmul_bitwise_vs_qc_matmul(L, ref2048, typ):
             np.testing.assert_array_equal(out.get(), ref, err_msg=f"type {typ} cols {cols} nt {nt}")
 
 
-def test_router_gemv_bitwise_at_model_shape(L, ref2048):
+@pytest.mark.parametrize("nt", (17, 2048))
+def test_router_gemv_bitwise_at_model_shape(L, ref2048, nt):
+    """The router of a verify batch (one warp per row) and of a prefill batch
+    (tiled kernel), both bitwise equal to qc_matmul."""
     rng = np.random.default_rng(0)
     router = rng.normal(0, 0.02, (512, 2048)).astype(np.float32)
-    x = rng.normal(0, 1, (17, 2048)).astype(np.float32)
+    x = rng.normal(0, 1, (nt, 2048)).astype(np.float32)
     dr, dx = L.Device(router), L.Device(x)
-    out = L.Device.empty((17, 512), np.float32)
-    L.call("matmul", out.p, dr.p, 0, 512, 2048, dx.p, 17)
+    out = L.Device.empty((nt, 512), np.float32)
+    L.call("matmul", out.p, dr.p, 0, 512, 2048, dx.p, nt)
     np.testing.assert_array_equal(out.get(), ref2048.matmul(router.view(np.uint8), 0, 512, 2048, x))
 
 
