@@ -255,39 +255,40 @@ __global__ void __launch_bounds__(1024) plan_kernel(const int *ids, const float 
         if (tid == kExperts - 1) pl.hdr->n_used = before + (c > 0);
     }
     if (tid == 0) pl.hdr->invalid_tokens = s_invalid;
-    // C: placement, one bitmap chunk of tokens at a time, ascending tokens.
+    // C: placement, one bitmap chunk of tokens at a time, ascending tokens: a
+    // pair's slot is its expert's running offset plus the chunk's tokens of that
+    // expert before it (set bits below it in the expert's bitmap).
     constexpr int W = kPlanChunk / 32;
     for (int c0 = 0; c0 < nt; c0 += kPlanChunk) {
         __syncthreads();
         for (int i = tid; i < kExperts * W; i += blockDim.x) bm[i] = 0;
         __syncthreads();
-        for (int t = c0 + tid; t < min(nt, c0 + kPlanChunk); t += blockDim.x) {
+        const int c1 = min(nt, c0 + kPlanChunk);
+        for (int t = c0 + tid; t < c1; t += blockDim.x) {
             if (pl.bad[t]) continue;
             for (int k = 0; k < kTop; k++) {
-                int e = ids[t * kTop + k];
+                const int e = ids[t * kTop + k];
                 if (e >= 0) atomicOr(&bm[e * W + (t - c0) / 32], 1u << ((t - c0) & 31));
             }
         }
         __syncthreads();
-        for (int e = warp; e < kExperts; e += blockDim.x / 32) {
-            unsigned word = lane < W ? bm[e * W + lane] : 0u;
-            int pc = __popc(word), pre = pc;
-#pragma unroll
-            for (int d = 1; d < 32; d <<= 1) {
-                int v = __shfl_up_sync(0xffffffffu, pre, d);
-                if (lane >= d) pre += v;
+        for (int t = c0 + tid; t < c1; t += blockDim.x) {
+            if (pl.bad[t]) continue;
+            const int wd = (t - c0) / 32;
+            const unsigned below = (1u << ((t - c0) & 31)) - 1u;
+            for (int k = 0; k < kTop; k++) {
+                const int e = ids[t * kTop + k];
+                if (e < 0) continue;
+                int pos = run[e] + __popc(bm[e * W + wd] & below);
+                for (int w2 = 0; w2 < wd; w2++) pos += __popc(bm[e * W + w2]);
+                pl.pairs[pos] = t * kTop + k;
             }
-            int total = __shfl_sync(0xffffffffu, pre, 31);
-            int pos = run[e] + pre - pc;
-            while (word) {
-                int b = __ffs(word) - 1;
-                word &= word - 1;
-                int t = c0 + lane * 32 + b, k = 0;
-                while (k < kTop && ids[t * kTop + k] != e) k++;
-                pl.pairs[pos++] = t * kTop + k;
-            }
-            __syncwarp();
-            if (lane == 0) run[e] += total;
+        }
+        __syncthreads();
+        for (int e = tid; e < kExperts; e += blockDim.x) {
+            int total = 0;
+            for (int w2 = 0; w2 < W; w2++) total += __popc(bm[e * W + w2]);
+            run[e] += total;
         }
     }
 }

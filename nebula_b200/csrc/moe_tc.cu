@@ -965,11 +965,13 @@ __global__ void tc_prep_kernel(const float *x, int H, __half *x16, float *xinv, 
     tc_prep_token(x + (size_t)t * H, H, x16 + (size_t)t * 2 * H, xinv + (size_t)t * 4, xsum + (size_t)t * (H / 32));
 }
 
-// One routed row per CTA: rows [0, n_pairs) are the plan's (token, expert)
+// One routed row per warp: rows [0, n_pairs) are the plan's (token, expert)
 // pairs in expert order, rows T*10 + t the shared expert's tokens.
-__global__ void tc_prep_rows_kernel(const float *x, int T, int H, const int *pairs, const int *n_pairs, __half *x16,
-                                    float *xinv, float *xsum) {
-    const int row = blockIdx.x;
+__global__ void __launch_bounds__(256) tc_prep_rows_kernel(const float *x, int T, int H, const int *pairs,
+                                                           const int *n_pairs, int rows, __half *x16, float *xinv,
+                                                           float *xsum) {
+    const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
+    if (row >= rows) return;
     int tok;
     if (row < T * kTop) {
         if (row >= __ldcg(n_pairs)) return;
@@ -977,8 +979,8 @@ __global__ void tc_prep_rows_kernel(const float *x, int T, int H, const int *pai
     } else {
         tok = row - T * kTop;
     }
-    tc_prep_token(x + (size_t)tok * H, H, x16 + (size_t)row * 2 * H, xinv + (size_t)row * 4,
-                  xsum + (size_t)row * (H / 32));
+    tc_prep_token_warp(x + (size_t)tok * H, H, x16 + (size_t)row * 2 * H, xinv + (size_t)row * 4,
+                       xsum + (size_t)row * (H / 32));
 }
 
 using EncodeTiled = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
@@ -1101,7 +1103,8 @@ int tc_prep_launch(const float *x, int T, int H, __half *x16, float *xinv, float
 int tc_prep_rows_launch(const float *x, int T, int H, const int *pairs, const int *n_pairs, bool shared, __half *x16,
                         float *xinv, float *xsum, cudaStream_t st) {
     const int rows = T * kTop + (shared ? T : 0);
-    tc_prep_rows_kernel<<<rows, 256, 0, st>>>(x, T, H, pairs, n_pairs, x16, xinv, xsum);
+    if (H % 128) return cudaErrorInvalidValue;
+    tc_prep_rows_kernel<<<(rows + 7) / 8, 256, 0, st>>>(x, T, H, pairs, n_pairs, rows, x16, xinv, xsum);
     return cudaGetLastError();
 }
 

@@ -137,4 +137,36 @@ __device__ inline void tc_prep_token(const float *x, int H, __half *x16, float *
     }
 }
 
+// The same preparation by one warp (H a multiple of 128): lane l holds values
+// 128i + 4l .. 4l+3; a 32-value group spans eight lanes.
+__device__ inline void tc_prep_token_warp(const float *x, int H, __half *x16, float *xinv, float *xsum) {
+    const int lane = threadIdx.x & 31;
+    float m = 0.0f;
+    for (int i = 0; i < H / 128; i++) {
+        const float4 v = __ldg(reinterpret_cast<const float4 *>(x + 128 * i) + lane);
+        m = fmaxf(m, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+    }
+#pragma unroll
+    for (int d = 16; d; d >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, d));
+    float s, inv;
+    pow2_scale(m, s, inv);
+    if (lane == 0) *xinv = inv;
+    for (int i = 0; i < H / 128; i++) {
+        const float4 v = __ldg(reinterpret_cast<const float4 *>(x + 128 * i) + lane);
+        const float f[4] = {v.x * s, v.y * s, v.z * s, v.w * s};
+        __half hi[4], lo[4];
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            hi[j] = __float2half_rn(f[j]);
+            lo[j] = __float2half_rn((f[j] - __half2float(hi[j])) * 2048.0f);
+        }
+        *reinterpret_cast<uint2 *>(x16 + 128 * i + 4 * lane) = *reinterpret_cast<uint2 *>(hi);
+        *reinterpret_cast<uint2 *>(x16 + H + 128 * i + 4 * lane) = *reinterpret_cast<uint2 *>(lo);
+        float g = (v.x + v.y) + (v.z + v.w);
+#pragma unroll
+        for (int d = 4; d; d >>= 1) g += __shfl_xor_sync(0xffffffffu, g, d);
+        if ((lane & 7) == 0) xsum[4 * i + (lane >> 3)] = g;
+    }
+}
+
 }  // namespace nb
