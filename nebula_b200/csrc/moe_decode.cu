@@ -4,14 +4,16 @@
 //  K1 dec_router_kernel: one CTA per 4 router rows (+ one for the shared
 //     gate row). Stages x and its rows in shared memory with TMA bulk copies
 //     and computes logits in the reference's 32-lane order (bitwise equal to
-//     qc_matmul, so expert ids are bit-exact). CTA t < T also writes x[t] in
-//     the pair-interleaved layout the expert kernel reads, plus its 32-value
-//     group sums. The last T CTAs to finish (atomic ticket) each run the
-//     top-10 routing of one token (qwen/gpu.cu:456-465 semantics) once all
-//     logits are in, and the last of them builds the plan: per-expert token
-//     lists in ascending token order, offsets, the used-expert list and
-//     per-token contribution counts. Without a router (qg_moe_routed) K1
-//     only stages x and the last CTA plans from the given ids/weights.
+//     qc_matmul, so expert ids are bit-exact). The last T CTAs to finish
+//     (atomic ticket) each run the top-10 routing of one token
+//     (qwen/gpu.cu:456-465 semantics) once all logits are in, and the last
+//     of them builds the plan: per-expert token lists in ascending token
+//     order, offsets, the used-expert list and per-token contribution counts.
+//     The first T CTAs to finish each write one token's activations in the
+//     layout the expert kernel reads (fp16 hi/lo or pair-interleaved, plus
+//     32-value group sums). Without a router (qg_moe_routed) CTA t < T
+//     writes x[t]'s activations and the last CTA plans from the given
+//     ids/weights.
 //
 //  K2 dec_experts_kernel: persistent, one CTA per SM of eight warps. Thread 0
 //     also produces: it claims work items from a device queue and streams
@@ -98,6 +100,21 @@ __global__ void __launch_bounds__(kK1Threads) dec_router_kernel(DecArgs a) {
     float *wr = xs + (size_t)a.T * a.H;           // [rows][H]
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int T = a.T, H = a.H;
+    // token t's activations in the layout the expert kernel reads (src: x[t])
+    auto prep_token = [&](int t, const float *src) {
+        if (a.use_tc) {
+            tc_prep_token(src, H, a.x16 + (size_t)t * 2 * H, a.xinv + (size_t)t * 4, a.xsum + (size_t)t * (H / 32));
+        } else {
+            float *dst = a.xpair + (size_t)t * H;
+            for (int i = tid; i < H; i += blockDim.x) dst[(i >> 6) * 64 + pair_pos<QG>(i & 63)] = src[i];
+            for (int g = warp; g < H / 32; g += blockDim.x / 32) {
+                float v = src[g * 32 + lane];
+#pragma unroll
+                for (int d = 16; d; d >>= 1) v += __shfl_xor_sync(0xffffffffu, v, d);
+                if (lane == 0) a.xsum[t * (H / 32) + g] = v;
+            }
+        }
+    };
     int row0 = 0, nrows = 0;
     if (a.router) {
         if (blockIdx.x < kExperts / kRouterRows) {
@@ -162,22 +179,7 @@ __global__ void __launch_bounds__(kK1Threads) dec_router_kernel(DecArgs a) {
                 }
             }
         }
-        if ((int)blockIdx.x < T) {
-            const int t = blockIdx.x;
-            const float *src = xs + (size_t)t * H;
-            if (a.use_tc) {
-                tc_prep_token(src, H, a.x16 + (size_t)t * 2 * H, a.xinv + (size_t)t * 4, a.xsum + (size_t)t * (H / 32));
-            } else {
-                float *dst = a.xpair + (size_t)t * H;
-                for (int i = tid; i < H; i += blockDim.x) dst[(i >> 6) * 64 + pair_pos<QG>(i & 63)] = src[i];
-                for (int g = warp; g < H / 32; g += blockDim.x / 32) {
-                    float v = src[g * 32 + lane];
-#pragma unroll
-                    for (int d = 16; d; d >>= 1) v += __shfl_xor_sync(0xffffffffu, v, d);
-                    if (lane == 0) a.xsum[t * (H / 32) + g] = v;
-                }
-            }
-        }
+        if ((int)blockIdx.x < T && !a.router) prep_token(blockIdx.x, xs + (size_t)blockIdx.x * H);
     }
     __threadfence();
     __syncthreads();
@@ -186,9 +188,15 @@ __global__ void __launch_bounds__(kK1Threads) dec_router_kernel(DecArgs a) {
     if (tid == 0) s_tk = atomicAdd(&a.ctr->k1_ticket, 1);
     __syncthreads();
     if (a.router) {
-        // The last T CTAs to finish route one token each, in parallel on their own
-        // SMs, once every CTA's logits are in (all K1 CTAs are resident, so the
-        // bounded wait only spans the last arrivals); the last of them plans.
+        // The first T CTAs to finish write one token's activations each; the last T
+        // route one token each, in parallel on their own SMs, once every CTA's logits
+        // are in (all K1 CTAs are resident, so the bounded wait only spans the last
+        // arrivals); the last of them plans. The grid has at least 128 CTAs and
+        // T <= 32, so the two groups are disjoint.
+        if (s_tk < T) {
+            prep_token(s_tk, a.x + (size_t)s_tk * H);
+            return;
+        }
         const int t = s_tk - (G - T);
         if (t < 0) return;
         if (tid == 0) s_last = wait_geq(&a.ctr->k1_ticket, G, &a.hdr->error);

@@ -796,18 +796,20 @@ __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a,
                     pp[0] = sv[j * kTcRows + rr];
                     pp[F] = sv[(kTok + j) * kTcRows + rr];
                 }
-                __threadfence();
+                // the CTA's stores, then one thread's fence and count (cumulative
+                // through the barrier); the last part's fence orders its reads after
                 bar_named(3, 256);
                 if (et == 0) {
+                    __threadfence();
                     int *cnt = a.gu_pcnt + it.sub * gu_mt + it.mt;
                     const int last = atomicAdd(cnt, 1) == it.np - 1;
                     if (last) *cnt = 0;
+                    __threadfence();
                     s_last = last;
                 }
                 bar_named(3, 256);
                 finish = s_last != 0;
                 if (finish) {
-                    __threadfence();
 #pragma unroll 1
                     for (int j = et >> 7; j < it.n; j += 2) {
                         const float *pp = a.gu_part + (size_t)tb.mrow[j] * kMaxParts * F2 + it.mt * kTcRows + rr;
@@ -869,9 +871,11 @@ __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a,
                     a.mid16[base] = hi;
                     a.mid16[base + F] = __float2half_rn((v - __half2float(hi)) * 2048.0f);
                 }
-                __threadfence();
                 bar_named(3, 256);
-                if (et == 0) atomicAdd(a.gu_done + it.sub, 1);
+                if (et == 0) {
+                    __threadfence();
+                    atomicAdd(a.gu_done + it.sub, 1);
+                }
             } else {
                 const int row = it.mt * kTcRows + rr;
                 if (a.ep_ranks) {
@@ -900,23 +904,24 @@ __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a,
                     if (it.expert < 0) a.shout[(size_t)tb.tok[j] * H + row] = y;
                     else a.slots[(size_t)tb.slot[j] * H + row] = y * tb.w[j];
                 }
-                __threadfence();
-                bar_named(3, 256);
                 if (et == 0) s_ncombine = 0;
                 bar_named(3, 256);
+                // per token: a fence (cumulative through the barrier) and the count; the
+                // last contribution's fence orders the combine's reads after it
                 if (et < it.n) {
                     const int t = tb.tok[et];
                     int *cnt = a.tilecnt + (size_t)t * dn_mt + it.mt;
                     const int expect = __ldcg(a.expect + t) & 0xffff;
+                    __threadfence();
                     if (atomicAdd(cnt, 1) == expect - 1) {
                         *cnt = 0;
+                        __threadfence();
                         s_combine[atomicAdd(&s_ncombine, 1)] = t;
                     }
                 }
                 bar_named(3, 256);
                 const int nc = s_ncombine;
                 if (nc) {
-                    __threadfence();
                     for (int ci = et >> 7; ci < nc; ci += 2) {
                         const int t = s_combine[ci];
                         const int rr = it.mt * kTcRows + (et & 127);
