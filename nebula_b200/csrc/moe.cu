@@ -1032,6 +1032,7 @@ DecArgs dec_args(int T, int H, int F, int gt, int dt, const float *x, float *out
     a.n_sub = reinterpret_cast<int *>(b + L.nsub);
     a.mid16 = reinterpret_cast<__half *>(b + L.mid16);
     a.midinv = reinterpret_cast<float *>(b + L.midinv);
+    a.xs16 = reinterpret_cast<__half *>(b + L.xs16);
     a.gu_part = reinterpret_cast<float *>(b + L.part);
     a.n_experts = kExperts;
     a.ep_shared_here = 1;

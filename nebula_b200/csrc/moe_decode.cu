@@ -103,7 +103,8 @@ __global__ void __launch_bounds__(kK1Threads) dec_router_kernel(DecArgs a) {
     // token t's activations in the layout the expert kernel reads (src: x[t])
     auto prep_token = [&](int t, const float *src) {
         if (a.use_tc) {
-            tc_prep_token(src, H, a.x16 + (size_t)t * 2 * H, a.xinv + (size_t)t * 4, a.xsum + (size_t)t * (H / 32));
+            tc_prep_token(src, H, a.x16 + (size_t)t * 2 * H, a.xinv + (size_t)t * 4, a.xsum + (size_t)t * (H / 32),
+                          a.xs16 + (size_t)t * (H / 16));
         } else {
             float *dst = a.xpair + (size_t)t * H;
             for (int i = tid; i < H; i += blockDim.x) dst[(i >> 6) * 64 + pair_pos<QG>(i & 63)] = src[i];
@@ -829,6 +830,7 @@ DecLayout dec_layout(int T, int H, int F) {
     L.shout = take(sizeof(float) * T * H);
     L.x16 = take(sizeof(__half) * T * 2 * H);
     L.xinv = take(sizeof(float) * T * 4);
+    L.xs16 = take(sizeof(__half) * T * 2 * (H / 32));
     L.sub = take(sizeof(SubJob) * (kExperts + 1));
     L.nsub = take(sizeof(int));
     L.mid16 = take(sizeof(__half) * (T * kTop + T) * 2 * F);
@@ -887,7 +889,7 @@ int dec_run(const DecArgs &in, cudaStream_t st, cudaEvent_t split) {
         t.gate = a.gate, t.up = a.up, t.down = a.down, t.sg = a.sg, t.su = a.su, t.sd = a.sd;
         t.grb = a.grb, t.drb = a.drb;
         t.all_tok = 1;
-        t.x16 = a.x16, t.xinv = a.xinv, t.xsum = a.xsum;
+        t.x16 = a.x16, t.xinv = a.xinv, t.xsum = a.xsum, t.xs16 = a.xs16;
         t.mi_stride = ((a.F / 128) + 3) & ~3;
         t.sub = a.sub, t.n_sub = a.n_sub, t.shared_subs = (a.sg && a.ep_shared_here) ? 1 : 0;
         t.sh_t0 = 0, t.sh_t1 = a.T;
@@ -902,8 +904,9 @@ int dec_run(const DecArgs &in, cudaStream_t st, cudaEvent_t split) {
         for (int p = 0; p < kMaxRanks; p++)
             t.ep_slots[p] = a.ep_slots[p], t.ep_shout[p] = a.ep_shout[p], t.ep_flags[p] = a.ep_flags[p];
         TcMaps maps;
-        if ((rc = tc_make_maps(t, maps, kMaxDecodeTokens))) return rc;
-        return tc_launch(t, maps, st, pdl, kMaxDecodeTokens);
+        const int tile = a.T <= kTcTokSmall ? kTcTokSmall : kMaxDecodeTokens;  // tokens per tile (all T)
+        if ((rc = tc_make_maps(t, maps, tile))) return rc;
+        return tc_launch(t, maps, st, pdl, tile);
     }
     const int ctas = sm_count();
     if (a.QG == 12 && a.QD == 12) return launch_k2<12, 12>(a, st, ctas, pdl);

@@ -25,7 +25,7 @@ constexpr size_t kPrefixBytes = (kHdrBytes + sizeof(DecCtr) + 255) & ~size_t(255
 
 struct DecLayout {
     size_t logits, sgate, ids, wts, xpair, xsum, off, used, pairs, expect, mid, msum, slots, shout;
-    size_t x16, xinv, sub, nsub, mid16, midinv, part, total;  // tensor-core path
+    size_t x16, xinv, xs16, sub, nsub, mid16, midinv, part, total;  // tensor-core path
 };
 DecLayout dec_layout(int T, int H, int F);
 
@@ -44,7 +44,7 @@ struct DecArgs {
     int *off, *used, *pairs, *expect;
     // tensor-core path (Q4_K): fp16 hi/lo activations and sub-jobs
     int use_tc;
-    __half *x16, *mid16;
+    __half *x16, *mid16, *xs16;
     float *xinv, *midinv;
     SubJob *sub;
     int *n_sub;

@@ -69,22 +69,32 @@ constexpr int kScRows = 2 * kTcRows * 16;         // d, dmin, m[8] per row per m
 // Layout of one instantiation for token tiles of up to TOK tokens.
 template <int TOK>
 struct Cfg {
+    // Decode tiles of kTcTokSmall tokens run the gate/up Q4_K min term
+    // dmin*sum_g m_g*sum(x over g) on the tensor cores: per superblock one more
+    // K=16 MMA per matrix, A'' = dmin*m_g*2^8 split hi/lo (exact in 22 bits), B'' =
+    // the 8 group sums of x*s/32 split hi/lo, accumulated over the whole item in
+    // D2 (read once per item) instead of per-superblock epilogue arithmetic.
+    static constexpr bool kMinD2 = TOK == kTcTokSmall;
     static constexpr int kBBytes = 2 * TOK * 128;             // B: TOK hi rows, then TOK lo rows, 128 B each
+    static constexpr int kB2Bytes = kMinD2 ? 64 * TOK : 0;    // B'': two K halves x [hi rows | lo rows] x 16 B
+    static constexpr int kBSlot = (kBBytes + kB2Bytes + 1023) & ~1023;
     static constexpr int kBStages = TOK <= 32 ? 4 : 3;        // B ring depth
     static constexpr int kScXs = 8 * TOK * 4;                 // the superblock's 8 group sums per row [row][8]
     static constexpr int kScSlot = kScRows + kScXs + 4 * TOK * 4;  // + scales [row][4]
     static constexpr int kVBytes = 2 * TOK * kTcRows * 4;     // one tile's outputs [plane][slot][row] (gate/up: g, u)
-    static constexpr int kOffB = kRawStages * kRawStage, kOffSc = kOffB + kBStages * kBBytes,
+    static constexpr int kOffB = kRawStages * kRawStage, kOffSc = kOffB + kBStages * kBSlot,
                          kOffV = kOffSc + 4 * kScSlot, kSmem = kOffV + kVBytes;
-    // Tensor memory (512 columns): D[db][m] at (db*2+m)*kDCols, A[ab][m] (32
-    // columns = 64 fp16 of one 64-value chunk) at kACol0 + (ab*2+m)*32; small
-    // tiles leave room for a deeper A ring.
+    // Tensor memory (512 columns): D[db][m] at (db*2+m)*kDCols; with the min term
+    // D2[m] at kD2Col + m*kDCols and A''[buf][m] (8 columns) at kA2Col +
+    // (buf*2+m)*8; A[ab][m] (32 columns = 64 fp16 of one 64-value chunk) at
+    // kACol0 + (ab*2+m)*32.
     static constexpr int kDCols = 2 * TOK;
-    static constexpr int kACol0 = 4 * kDCols;
-    static constexpr int kAStages = (512 - kACol0) / 64 >= 4 ? 4 : 2;
-    static_assert(kACol0 + kAStages * 64 <= 512, "tensor memory budget");
+    static constexpr int kD2Col = 4 * kDCols, kA2Col = kD2Col + 2 * kDCols;
+    static constexpr int kACol0 = kMinD2 ? kA2Col + 32 : 4 * kDCols;
+    static constexpr int kAStages = (512 - kACol0) / 64 >= 4 ? 4 : (512 - kACol0) / 64;
+    static_assert(kAStages >= 2 && kACol0 + kAStages * 64 <= 512, "tensor memory budget");
     static_assert(kSmem % 16 == 0 && kScSlot % 16 == 0 && kOffB % 1024 == 0 && kBBytes % 1024 == 0 &&
-                      (TOK * 128) % 1024 == 0, "alignment");
+                      kBSlot % 1024 == 0 && (TOK * 128) % 1024 == 0 && (16 * TOK) % 128 == 0, "alignment");
 };
 constexpr int kTokDecode = 32;  // decode: every token tile has at most kMaxDecodeTokens tokens
 static_assert(kTokDecode <= kTcTok, "tile sizes");
@@ -105,6 +115,7 @@ struct Bars {
     uint64_t d_full[2], d_empty[2];
     uint64_t sc_full[4], sc_empty[4];
     uint64_t mma_done[2];
+    uint64_t d2_empty;  // the epilogue has read D2 (gate/up items, min term on the tensor cores)
 };
 
 __device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
@@ -221,6 +232,11 @@ __device__ __forceinline__ void tmem_st32(uint32_t addr, const uint32_t (&r)[32]
         "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
         : "memory");
 }
+__device__ __forceinline__ void tmem_st8(uint32_t addr, const uint32_t (&r)[8]) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(addr), "r"(r[0]), "r"(r[1]),
+                 "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
+                 : "memory");
+}
 __device__ __forceinline__ void tmem_st16(uint32_t addr, const uint32_t (&r)[16]) {
     asm volatile(
         "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(addr),
@@ -291,6 +307,26 @@ __device__ __forceinline__ uint4 q4k_row_scales(const unsigned char *row) {
     return make_uint4(__float_as_uint(d), __float_as_uint(dmin), m4[0], m4[1]);
 }
 
+// The min term of one superblock row as a K=16 A operand (8 tensor-memory
+// columns): values 0..7 are the fp16 hi parts of dmin*m_g*2^8 for g = 0..7,
+// values 8..15 the lo parts (v - hi; v has at most 17 significant bits, so the
+// pair is exact unless dmin is below about 2^-16). The B operand pairs both
+// halves with the same group sums.
+__device__ __forceinline__ void q4k_min_a(const unsigned char *row, uint32_t (&o)[8]) {
+    const uint4 rs = q4k_row_scales(row);  // d, dmin, m[8]
+    const float dm = __uint_as_float(rs.y) * 256.0f;
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const int g0 = 2 * i, g1 = 2 * i + 1;
+        const float v0 = dm * (float)(((g0 < 4 ? rs.z : rs.w) >> (8 * (g0 & 3))) & 0xFFu);
+        const float v1 = dm * (float)(((g1 < 4 ? rs.z : rs.w) >> (8 * (g1 & 3))) & 0xFFu);
+        const __half h0 = __float2half_rn(v0), h1 = __float2half_rn(v1);
+        const __half l0 = __float2half_rn(v0 - __half2float(h0)), l1 = __float2half_rn(v1 - __half2float(h1));
+        o[i] = (uint32_t)__half_as_ushort(h0) | ((uint32_t)__half_as_ushort(h1) << 16);
+        o[4 + i] = (uint32_t)__half_as_ushort(l0) | ((uint32_t)__half_as_ushort(l1) << 16);
+    }
+}
+
 // sum_g m_g * xs[row][g] for rows j0 and j1 (xs: 8 group sums per row)
 __device__ __forceinline__ float2 mterm2(const float (&mg)[8], const float *xs, int j0, int j1) {
     const float4 a0 = *reinterpret_cast<const float4 *>(xs + j0 * 8), a1 = *reinterpret_cast<const float4 *>(xs + j0 * 8 + 4);
@@ -356,6 +392,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a,
             mbar_init(&bars.d_empty[i], kEpiWarps);
             mbar_init(&bars.mma_done[i], 1);
         }
+        mbar_init(&bars.d2_empty, kEpiWarps);
         for (int i = 0; i < kBStages; i++) {
             mbar_init(&bars.b_full[i], 1);
             mbar_init(&bars.b_empty[i], 2);
@@ -468,8 +505,9 @@ __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a,
         // issuer mi: gate/up tiles -> matrix mi; down tiles -> chunks 2mi, 2mi+1
         if (lane == 0) {
             const int mi = warp == kMmaWarp ? 0 : 1;
-            int gsb = 0, gch = 0;
+            int gsb = 0, gch = 0, gu_items = 0;
             const uint64_t b_desc0 = umma_desc_sw128(smem_u32(smem + kOffB));
+            const uint64_t b2_desc0 = umma_desc(smem_u32(smem + kOffB + kBBytes), 32 * kTok, 128);
             const uint32_t idesc = idesc_f16(kTcRows, 2 * kTok);  // hi and lo rows of every tile row
             for (int seq = 0;; seq++) {
                 const int slot = seq & 3;
@@ -491,11 +529,22 @@ __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a,
                         if (gu || (c >> 1) == mi) {
                             tc_fence_after();
                             const uint32_t ac = tmem + (uint32_t)(kACol0 + (ab * 2 + (gu ? mi : 0)) * 32);
-                            const uint64_t bd = b_desc0 + (uint64_t)((bs * kBBytes) >> 4);
+                            const uint64_t bd = b_desc0 + (uint64_t)((bs * C::kBSlot) >> 4);
                             mma_ts(d, ac, bd, idesc, gu ? c != 0 : (c & 1) != 0);
                             mma_ts1(d, ac + 8, bd + 2, idesc);
                             mma_ts1(d, ac + 16, bd + 4, idesc);
                             mma_ts1(d, ac + 24, bd + 6, idesc);
+                            if constexpr (C::kMinD2) {
+                                if (gu && c == 3) {  // min term into D2 (the item's first superblock starts it)
+                                    if (sb == 0 && gu_items > 0 &&
+                                        !(ok = wait_phase(&bars.d2_empty, (gu_items - 1) & 1, &abort_flag, err)))
+                                        break;
+                                    tc_fence_after();
+                                    mma_ts(tmem + (uint32_t)(C::kD2Col + mi * kDCols),
+                                           tmem + (uint32_t)(C::kA2Col + ((gsb & 1) * 2 + mi) * 8),
+                                           b2_desc0 + (uint64_t)((bs * C::kBSlot) >> 4), idesc, sb != 0);
+                                }
+                            }
                             mma_commit(&bars.a_empty[ab]);
                             mma_commit(&bars.b_empty[bs]);
                         } else {  // the other issuer's chunk: nothing read here
@@ -505,6 +554,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a,
                     }
                     if (ok) mma_commit(&bars.d_full[db]);
                 }
+                if (gu) gu_items++;
                 arrive(&bars.item_empty[slot]);
                 if (!ok) break;
             }
@@ -524,7 +574,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a,
             if (it.kind == kEnd) break;
             TokTab<TOK> &tb = tabs[slot];
             const bool gu = it.kind == kGU, sh = it.expert < 0;
-            const int n_pad = (it.n + 15) & ~15;
+            const int n_pad = min(kTok, (it.n + 15) & ~15);  // table entries filled (padding repeats row 0)
             const int row0 = sh ? T * kTop + it.tok0 : it.first;  // first SwiGLU-output row of the tile
             for (int j = lane; j < n_pad; j += 32) {
                 const int jv = j < it.n ? j : 0;
@@ -562,10 +612,18 @@ __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a,
                         if (gch >= kBStages &&
                             !(ok = wait_phase(&bars.b_empty[bs], (gch / kBStages - 1) & 1, &abort_flag, err)))
                             break;
-                        unsigned char *bt = smem + kOffB + bs * kBBytes;
-                        mbar_arrive_expect_tx(&bars.b_full[bs], kBBytes);
+                        unsigned char *bt = smem + kOffB + bs * C::kBSlot;
+                        const bool b2 = C::kMinD2 && gu && c == 3;  // with the superblock's min-term B
+                        mbar_arrive_expect_tx(&bars.b_full[bs], kBBytes + (b2 ? C::kB2Bytes : 0));
                         tma_2d(bt, bh, (gsbk * 4 + c) * 64, brow, &bars.b_full[bs]);
                         tma_2d(bt + kTok * 128, bl, (gsbk * 4 + c) * 64, brow, &bars.b_full[bs]);
+                        if (b2) {  // [K half][hi rows | lo rows] x 8 group sums, both halves the same
+                            for (int kh = 0; kh < 2; kh++) {
+                                tma_2d(bt + kBBytes + kh * 32 * kTok, &maps.gx_hi, gsbk * 8, brow, &bars.b_full[bs]);
+                                tma_2d(bt + kBBytes + kh * 32 * kTok + 16 * kTok, &maps.gx_lo, gsbk * 8, brow,
+                                       &bars.b_full[bs]);
+                            }
+                        }
                     }
                 }
                 arrive(&bars.item_empty[slot]);
@@ -623,6 +681,15 @@ __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a,
                             tmem_st16(a_lanes + (uint32_t)((ab * 2 + m) * 32), r);
                         }
                     }
+                    if constexpr (C::kMinD2) {
+                        if (mats == 2 && c + kGrp > 3) {  // with chunk 3: matrix nib's min-term A for this superblock
+                            uint32_t o[8];
+                            q4k_min_a(raw + nib * kSbBytes + ct * 144, o);
+                            tmem_st8(tmem + ((uint32_t)(32 * (warp & 3)) << 16) +
+                                         (uint32_t)(C::kA2Col + ((gsb & 1) * 2 + nib) * 8),
+                                     o);
+                        }
+                    }
                     tmem_wait_st();
                     tc_fence_before();
                     __syncwarp();
@@ -645,7 +712,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a,
         const int r = 32 * q + lane;             // row within the tile
         const int half = ew >> 2;                // token half
         const int et = tid - kEpiWarp0 * 32;     // 0..255
-        constexpr int kHalf = kTok / 2;        // tokens per half, at most
+        constexpr int kHalf = (kTok / 2 + 7) / 8 * 8;  // token slots per half, at most (multiple of 8)
         int gsb = 0;
         for (int seq = 0;; seq++) {
             const int slot = seq & 3;
@@ -668,6 +735,12 @@ __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a,
             for (int m = 0; m < 2; m++)
 #pragma unroll
                 for (int p = 0; p < kHalf / 2; p++) acc[m][p] = make_float2(0.0f, 0.0f);
+            // min term on the tensor cores (gate/up): thread = row x matrix `half`, one
+            // sum per D column (token of all T, or row of the tile)
+            const int ncol = by_tok ? T : it.n;
+            float acc2[C::kMinD2 ? kTok : 1];
+#pragma unroll
+            for (int i = 0; i < (C::kMinD2 ? kTok : 1); i++) acc2[i] = 0.0f;
             for (int sb = 0; sb < nsb && ok; sb++, gsb++) {
                 const int db = gsb & 1, sc_slot = gsb & 3;
                 if (!(ok = wait_phase(&bars.d_full[db], (gsb >> 1) & 1, &abort_flag, err))) break;
@@ -679,7 +752,26 @@ __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a,
                 const float *inv4 = reinterpret_cast<const float *>(scb + kScRows + kScXs);  // [row][4]
                 const uint32_t lanes = tmem + ((uint32_t)(32 * q) << 16);
                 const float2 k2048 = make_float2(1.0f / 2048.0f, 1.0f / 2048.0f);
-                if (gu) {
+                if (C::kMinD2 && gu) {
+                    if constexpr (C::kMinD2) {
+                        const float dsc = __uint_as_float(scs[half * kTcRows + r].x);
+                        const uint32_t col0 = lanes + (uint32_t)((db * 2 + half) * kDCols);
+#pragma unroll
+                        for (int cb = 0; cb < kTok / 8; cb++) {
+                            if (cb * 8 < ncol) {
+                                uint32_t rh[8], rl[8];
+                                tmem_ld8_nw(col0 + cb * 8, rh);
+                                tmem_ld8_nw(col0 + kTok + cb * 8, rl);
+                                tmem_wait_ld();
+#pragma unroll
+                                for (int i = 0; i < 8; i++)
+                                    acc2[cb * 8 + i] = __fmaf_rn(
+                                        dsc, __fmaf_rn(__uint_as_float(rl[i]), 1.0f / 2048.0f, __uint_as_float(rh[i])),
+                                        acc2[cb * 8 + i]);
+                            }
+                        }
+                    }
+                } else if (gu) {
 #pragma unroll
                     for (int m = 0; m < 2; m++) {
                         const uint4 sv = scs[m * kTcRows + r];
@@ -761,10 +853,44 @@ __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a,
                     arrive(&bars.sc_empty[sc_slot]);
                 }
             }
+            if constexpr (C::kMinD2) {
+                if (gu) {  // the item's min term: D2, complete once its last superblock's D is
+                    if (ok) {
+                        tc_fence_after();
+                        const uint32_t c2 = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(C::kD2Col + half * kDCols);
+#pragma unroll
+                        for (int cb = 0; cb < kTok / 8; cb++) {
+                            if (cb * 8 < ncol) {
+                                uint32_t rh[8], rl[8];
+                                tmem_ld8_nw(c2 + cb * 8, rh);
+                                tmem_ld8_nw(c2 + kTok + cb * 8, rl);
+                                tmem_wait_ld();
+#pragma unroll
+                                for (int i = 0; i < 8; i++)
+                                    acc2[cb * 8 + i] = __fmaf_rn(
+                                        -0.125f, __fmaf_rn(__uint_as_float(rl[i]), 1.0f / 2048.0f, __uint_as_float(rh[i])),
+                                        acc2[cb * 8 + i]);
+                            }
+                        }
+                        tc_fence_before();
+                    }
+                    __syncwarp();
+                    if (lane == 0) arrive(&bars.d2_empty);
+                }
+            }
             ok = ok && wait_phase(&bars.tab_full[slot], (seq >> 2) & 1, &abort_flag, err);
             if (!bar_all(3, 256, ok)) break;
             // the tile's outputs (SwiGLU for gate/up) to the shared buffer sv[slot][row]
+            // (with the min term on the tensor cores: sv[matrix][column][row], scaled
+            // back by the column's 1/s)
             float *sv = reinterpret_cast<float *>(smem + kOffV);
+            const bool cols_tok = C::kMinD2 && gu && by_tok;  // gate/up planes indexed by token
+            if (C::kMinD2 && gu) {
+                const int xrow0 = by_tok ? 0 : (it.expert < 0 ? T * kTop + it.tok0 : it.first);
+#pragma unroll
+                for (int c = 0; c < (C::kMinD2 ? kTok : 1); c++)
+                    if (c < ncol) sv[(half * kTok + c) * kTcRows + r] = acc2[c] * __ldcg(a.xinv + (size_t)(xrow0 + c) * 4);
+            } else {
 #pragma unroll
             for (int cb = 0; cb < kHalf / 8; cb++) {
                 if (cb * 8 < hw) {
@@ -783,6 +909,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a,
                     }
                 }
             }
+            }
             bar_named(3, 256);
             const int rr = et & 127;  // row handled by this thread in the per-token loops
             bool finish = true;
@@ -792,9 +919,10 @@ __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a,
                 const size_t F2 = 2 * (size_t)F;
 #pragma unroll 1
                 for (int j = et >> 7; j < it.n; j += 2) {
+                    const int cj = cols_tok ? tb.tok[j] : j;
                     float *pp = a.gu_part + ((size_t)tb.mrow[j] * kMaxParts + it.kq) * F2 + it.mt * kTcRows + rr;
-                    pp[0] = sv[j * kTcRows + rr];
-                    pp[F] = sv[(kTok + j) * kTcRows + rr];
+                    pp[0] = sv[cj * kTcRows + rr];
+                    pp[F] = sv[(kTok + cj) * kTcRows + rr];
                 }
                 // the CTA's stores, then one thread's fence and count (cumulative
                 // through the barrier); the last part's fence orders its reads after
@@ -818,8 +946,9 @@ __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a,
                             g += __ldcg(pp + q * F2);
                             u += __ldcg(pp + q * F2 + F);
                         }
-                        sv[j * kTcRows + rr] = g;
-                        sv[(kTok + j) * kTcRows + rr] = u;
+                        const int cj = cols_tok ? tb.tok[j] : j;
+                        sv[cj * kTcRows + rr] = g;
+                        sv[(kTok + cj) * kTcRows + rr] = u;
                     }
                 }
                 bar_named(3, 256);
@@ -832,8 +961,9 @@ __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a,
 #pragma unroll 1
                 for (int j = ew; j < it.n; j += kEpiWarps) {
                     // SwiGLU of the token's 128 rows, kept in plane 0 for the split below
-                    float *vj = sv + j * kTcRows;
-                    const float *uj = sv + (kTok + j) * kTcRows;
+                    const int cj = cols_tok ? tb.tok[j] : j;
+                    float *vj = sv + cj * kTcRows;
+                    const float *uj = sv + (kTok + cj) * kTcRows;
                     float v[4];
 #pragma unroll
                     for (int i = 0; i < 4; i++) {
@@ -865,7 +995,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a,
                 // fp16 hi/lo split of v*s for the down tiles
 #pragma unroll 1
                 for (int j = et >> 7; j < it.n; j += 2) {
-                    const float v = sv[j * kTcRows + rr] * s_scale[j];
+                    const float v = sv[(cols_tok ? tb.tok[j] : j) * kTcRows + rr] * s_scale[j];
                     const __half hi = __float2half_rn(v);
                     const size_t base = (size_t)tb.mrow[j] * 2 * F + it.mt * kTcRows + rr;
                     a.mid16[base] = hi;
@@ -1070,6 +1200,10 @@ int tc_make_maps(const TcArgs &a, TcMaps &m, int tok) {
     if (!rc) rc = make_map_2d(&m.bm_hi, f16, 2, a.mid16, F, rows, 4 * F, 64, tok, sw);
     if (!rc) rc = make_map_2d(&m.bm_lo, f16, 2, a.mid16 + F, F, rows, 4 * F, 64, tok, sw);
     if (!rc) rc = make_map_2d(&m.sx, f32, 4, a.xsum, H / 32, xrows, H / 8, 8, tok, none);
+    if (!rc && a.xs16) rc = make_map_2d(&m.gx_hi, f16, 2, a.xs16, H / 32, xrows, H / 8, 8, tok, none);
+    if (!rc && a.xs16) rc = make_map_2d(&m.gx_lo, f16, 2, a.xs16 + H / 32, H / 32, xrows, H / 8, 8, tok, none);
+    if (!rc && !a.xs16) m.gx_hi = m.gx_lo = m.sx;
+    if (!rc && tok == kTcTokSmall && !a.xs16) rc = cudaErrorInvalidValue;  // the min term needs the fp16 group sums
     if (!rc) rc = make_map_2d(&m.sm, f32, 4, a.msum, F / 32, rows, F / 8, 8, tok, none);
     if (!rc) rc = make_map_2d(&m.ix, f32, 4, a.xinv, 4, xrows, 16, 4, tok, none);
     if (!rc) rc = make_map_2d(&m.im, f32, 4, a.midinv, a.mi_stride, rows, 4 * (size_t)a.mi_stride, 4, tok, none);
@@ -1095,6 +1229,7 @@ int tc_launch_tok(const TcArgs &a, const TcMaps &m, cudaStream_t st, bool pdl) {
 }
 
 int tc_launch(const TcArgs &a, const TcMaps &m, cudaStream_t st, bool pdl, int max_tile) {
+    if (max_tile <= kTcTokSmall) return tc_launch_tok<kTcTokSmall>(a, m, st, pdl);
     if (max_tile <= kTokDecode) return tc_launch_tok<kTokDecode>(a, m, st, pdl);
     if (max_tile <= kTcTok) return tc_launch_tok<kTcTok>(a, m, st, pdl);
     return cudaErrorInvalidValue;

@@ -6,6 +6,7 @@
 namespace nb {
 
 constexpr int kTcTok = 48;     // tokens per sub-job (token tile of one expert)
+constexpr int kTcTokSmall = 24;  // decode tiles with the Q4_K min term on the tensor cores
 constexpr int kTcRows = 128;   // weight rows per tile (MMA M)
 constexpr int kMaxRanks = 8;   // expert-parallel ranks (GPUs of one box)
 constexpr int kMaxParts = 3;   // K parts of one gate/up tile (balanced gate/up work)
@@ -27,6 +28,7 @@ struct TcArgs {
     const __half *x16;     // [T or rows][2][H]: x*s hi, (x*s - hi)*2048 lo, s a power of two per row
     const float *xinv;     // [T or rows][4]: 1/s in element 0
     const float *xsum;     // [T or rows][H/32]: 32-value group sums of x
+    const __half *xs16;    // [T][2][H/32] (24-token decode tiles): group sums * s/32, hi and lo as x16
     const SubJob *sub;     // shared sub-jobs first, then routed
     const int *n_sub;      // device count of sub-jobs
     int shared_subs;       // number of shared sub-jobs (known before routing)
@@ -77,6 +79,7 @@ struct TcMaps {
     CUtensorMap gate, up, down, sg, su, sd;  // raw Q4_K rows, one superblock x 128 rows per box
     CUtensorMap bx_hi, bx_lo, bm_hi, bm_lo;  // B rows (activations, SwiGLU outputs), 64 values x tile rows, 128B swizzle
     CUtensorMap sx, sm, ix, im;              // their group sums (8 x tile rows) and scales (4 x tile rows)
+    CUtensorMap gx_hi, gx_lo;                // xs16 hi and lo planes (8 x tile rows, no swizzle)
 };
 
 bool tc_supported(int H, int F, int QG, int QD);
@@ -106,8 +109,10 @@ __device__ __forceinline__ void pow2_scale(float mx, float &s, float &inv) {
 }
 
 // Per-token preparation shared by the decode router kernel and the prep kernel:
-// scale to max|x*s| in [2^13, 2^14), split into fp16 hi/lo, 32-value group sums.
-__device__ inline void tc_prep_token(const float *x, int H, __half *x16, float *xinv, float *xsum) {
+// scale to max|x*s| in [2^13, 2^14), split into fp16 hi/lo, 32-value group sums
+// (and, when xs16 is given, the group sums times s/32 split into fp16 hi/lo).
+__device__ inline void tc_prep_token(const float *x, int H, __half *x16, float *xinv, float *xsum,
+                                     __half *xs16 = nullptr) {
     __shared__ float red[32];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
     float m = 0.0f;
@@ -133,7 +138,15 @@ __device__ inline void tc_prep_token(const float *x, int H, __half *x16, float *
         float v = x[g * 32 + lane];
 #pragma unroll
         for (int d = 16; d; d >>= 1) v += __shfl_xor_sync(0xffffffffu, v, d);
-        if (lane == 0) xsum[g] = v;
+        if (lane == 0) {
+            xsum[g] = v;
+            if (xs16) {
+                const float w = v * s * 0.03125f;
+                const __half hi = __float2half_rn(w);
+                xs16[g] = hi;
+                xs16[H / 32 + g] = __float2half_rn((w - __half2float(hi)) * 2048.0f);
+            }
+        }
     }
 }
 
