@@ -33,7 +33,6 @@ from __future__ import annotations
 import argparse
 import json
 import os
-import subprocess
 import sys
 import time
 from pathlib import Path
@@ -70,56 +69,87 @@ def measured_peaks() -> dict:
     return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
 
 
-class Clocks:
-    """nvidia-smi sampling during the timed region."""
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+def pci_bus_id(torch, index: int) -> str | None:
+    """NVML's PCI bus id of CUDA device `index` (CUDA and NVML may number GPUs differently)."""
+    try:
+        pr = torch.cuda.get_device_properties(index)
+        return f"{pr.pci_domain_id:08x}:{pr.pci_bus_id:02x}:{pr.pci_device_id:02x}.0"
+    except (AttributeError, RuntimeError):
+        return None
 
-    def __init__(self, index: int):
-        self.index = index
-        self.proc = None
+
+class Clocks:
+    """SM clock and throttle-reason sampling during the timed region.
+
+    NVML is polled from a thread every 5 ms (a timed region of a few steps is
+    shorter than nvidia-smi's own sampling period); the samples are also
+    written as CSV next to the other run outputs. Reading only: no setting of
+    the GPU is changed."""
+    REASONS = (("hw_slowdown", 8), ("hw_thermal_slowdown", 64), ("sw_thermal_slowdown", 32),
+               ("sw_power_cap", 4))
+
+    def __init__(self, index: int, pci_bus_id: str | None = None):
+        self.index, self.pci = index, pci_bus_id
+        self.samples: list[tuple[float, float, float, int]] = []
+        self.max_mhz = None
         self.path = ROOT / "gpurun_out" / f"clocks_rank{index}.csv"
+        self.thread = None
+        self.stop = None
+
+    def _handle(self, nv):
+        if self.pci:
+            try:
+                return nv.nvmlDeviceGetHandleByPciBusId(self.pci)
+            except nv.NVMLError:
+                pass
+        return nv.nvmlDeviceGetHandleByIndex(self.index)
 
     def __enter__(self):
+        import threading
         try:
-            self.path.parent.mkdir(exist_ok=True)
-            self.fh = open(self.path, "w")
-            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
-                                          "--format=csv,noheader,nounits", "-lms", "100"],
-                                         stdout=self.fh, stderr=subprocess.DEVNULL)
-        except (OSError, FileNotFoundError):
-            self.proc = None
+            import pynvml as nv
+            nv.nvmlInit()
+            h = self._handle(nv)
+            self.max_mhz = float(nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM))
+        except Exception:  # no NVML: the summary says so
+            return self
+        self.stop = threading.Event()
+
+        def poll():
+            t0 = time.perf_counter()
+            while not self.stop.is_set():
+                try:
+                    mhz = float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM))
+                    why = int(nv.nvmlDeviceGetCurrentClocksEventReasons(h))
+                    watts = nv.nvmlDeviceGetPowerUsage(h) / 1000.0
+                except Exception:
+                    break
+                self.samples.append((time.perf_counter() - t0, mhz, watts, why))
+                self.stop.wait(0.005)
+
+        self.thread = threading.Thread(target=poll, daemon=True)
+        self.thread.start()
         return self
 
     def __exit__(self, *exc):
-        if self.proc:
-            self.proc.terminate()
+        if self.thread:
+            self.stop.set()
+            self.thread.join(5)
             try:
-                self.proc.wait(5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
-            self.fh.close()
+                self.path.parent.mkdir(exist_ok=True)
+                with open(self.path, "w") as f:
+                    f.write("t_s,sm_mhz,sm_max_mhz,power_w,reasons_mask\n")
+                    for t, mhz, w, why in self.samples:
+                        f.write(f"{t:.4f},{mhz:.0f},{self.max_mhz:.0f},{w:.1f},{why:#x}\n")
+            except OSError:
+                pass
 
     def summary(self) -> dict:
-        if not self.path.exists():
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"]}
-        sm, mx, reasons = [], None, set()
-        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
-        for line in self.path.read_text().splitlines():
-            f = [c.strip() for c in line.split(",")]
-            if len(f) < 9:
-                continue
-            try:
-                sm.append(float(f[1]))
-                mx = float(f[2])
-            except ValueError:
-                continue
-            for name, v in zip(names, f[5:9]):
-                if v.lower().startswith("active"):
-                    reasons.add(name)
-        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sm)}
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["unavailable"], "samples": 0}
+        reasons = sorted({name for _, _, _, why in self.samples for name, bit in self.REASONS if why & bit})
+        return {"sm_mhz": float(np.median([s[1] for s in self.samples])), "sm_max_mhz": self.max_mhz,
+                "reasons": reasons, "samples": len(self.samples), "source": "NVML, 5 ms period"}
 
 
 class Stack:
@@ -275,7 +305,7 @@ def run_reference_arm(args, rank: int, world: int) -> None:
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=("ours", "reference"))
     ap.add_argument("--layers", type=int, default=48)
@@ -320,7 +350,7 @@ def main() -> None:
     used = stack.experts_used()
 
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with Clocks(local) as clk:
+    with Clocks(local, pci_bus_id(torch, local)) as clk:
         barrier()
         start.record()
         for _ in range(args.steps):
