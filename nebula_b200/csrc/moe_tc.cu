@@ -215,6 +215,11 @@ __device__ __forceinline__ void tmem_ld8_nw(uint32_t addr, uint32_t (&r)[8]) {
                  : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
                  : "r"(addr));
 }
+__device__ __forceinline__ void tmem_ld4_nw(uint32_t addr, uint32_t (&r)[4]) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(addr));
+}
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ uint32_t tmem_ld1(uint32_t addr) {
     uint32_t r;
@@ -752,7 +757,66 @@ __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a,
                 const float *inv4 = reinterpret_cast<const float *>(scb + kScRows + kScXs);  // [row][4]
                 const uint32_t lanes = tmem + ((uint32_t)(32 * q) << 16);
                 const float2 k2048 = make_float2(1.0f / 2048.0f, 1.0f / 2048.0f);
-                if (C::kMinD2 && gu) {
+                bool d_released = false;
+                if (TOK == 48 && gu && !by_tok) {
+                    // 48-token tiles of per-row activations (prefill): each 4-slot block loads
+                    // both matrices' hi/lo columns with one wait, then runs 8 independent
+                    // per-slot chains; the D buffer is released once its last load has landed.
+                    // Slots between the item's rows and the block end read finite padding
+                    // data and are never stored.
+                    float dsc[2], nmn[2], mg[2][8];
+#pragma unroll
+                    for (int m = 0; m < 2; m++) {
+                        const uint4 sv = scs[m * kTcRows + r];
+                        dsc[m] = __uint_as_float(sv.x);
+                        nmn[m] = -__uint_as_float(sv.y);
+#pragma unroll
+                        for (int g = 0; g < 8; g++) mg[m][g] = (float)(((g < 4 ? sv.z : sv.w) >> (8 * (g & 3))) & 0xFFu);
+                    }
+                    const uint32_t colg = lanes + (uint32_t)((db * 2) * kDCols), colu = colg + kDCols;
+                    const int ncb = min(kHalf / 4, (hw + 3) >> 2);
+#pragma unroll
+                    for (int cb = 0; cb < kHalf / 4; cb++) {
+                        if (cb >= ncb) break;
+                        uint32_t gh[4], gl[4], uh[4], ul[4];
+                        const uint32_t o = (uint32_t)(j0 + cb * 4);
+                        tmem_ld4_nw(colg + o, gh);
+                        tmem_ld4_nw(colg + kTok + o, gl);
+                        tmem_ld4_nw(colu + o, uh);
+                        tmem_ld4_nw(colu + kTok + o, ul);
+                        tmem_wait_ld();
+                        if (cb == ncb - 1) {
+                            tc_fence_before();
+                            __syncwarp();
+                            if (lane == 0) arrive(&bars.d_empty[db]);
+                            d_released = true;
+                        }
+#pragma unroll
+                        for (int i = 0; i < 4; i++) {
+                            const int j = j0 + cb * 4 + i;
+                            const float inv = inv4[j * 4];
+                            const float4 xa = *reinterpret_cast<const float4 *>(xs + j * 8);
+                            const float4 xb = *reinterpret_cast<const float4 *>(xs + j * 8 + 4);
+                            const float hv[2] = {__uint_as_float(gh[i]), __uint_as_float(uh[i])};
+                            const float lv[2] = {__uint_as_float(gl[i]), __uint_as_float(ul[i])};
+#pragma unroll
+                            for (int m = 0; m < 2; m++) {
+                                const float dot = __fmul_rn(__fmaf_rn(lv[m], 1.0f / 2048.0f, hv[m]), inv);
+                                float t = __fmul_rn(mg[m][0], xa.x);
+                                t = __fmaf_rn(mg[m][1], xa.y, t);
+                                t = __fmaf_rn(mg[m][2], xa.z, t);
+                                t = __fmaf_rn(mg[m][3], xa.w, t);
+                                t = __fmaf_rn(mg[m][4], xb.x, t);
+                                t = __fmaf_rn(mg[m][5], xb.y, t);
+                                t = __fmaf_rn(mg[m][6], xb.z, t);
+                                t = __fmaf_rn(mg[m][7], xb.w, t);
+                                float2 &ac = acc[m][cb * 2 + (i >> 1)];
+                                float &a1 = (i & 1) ? ac.y : ac.x;
+                                a1 = __fmaf_rn(nmn[m], t, __fmaf_rn(dsc[m], dot, a1));
+                            }
+                        }
+                    }
+                } else if (C::kMinD2 && gu) {
                     if constexpr (C::kMinD2) {
                         const float dsc = __uint_as_float(scs[half * kTcRows + r].x);
                         const uint32_t col0 = lanes + (uint32_t)((db * 2 + half) * kDCols);
@@ -849,7 +913,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a,
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) {
-                    arrive(&bars.d_empty[db]);
+                    if (!d_released) arrive(&bars.d_empty[db]);
                     arrive(&bars.sc_empty[sc_slot]);
                 }
             }
