@@ -354,6 +354,8 @@ struct __align__(16) TokTab {
     int mrow[TOK];  // SwiGLU-output row written (gate/up) or read (down)
     int slot[TOK];  // routed slot t*10+k (down)
     float w[TOK];   // route weight (down)
+    float xi[TOK];  // 1/s of each D column's activation row (gate/up with the min term on the tensor cores)
+    int ex[TOK];    // expected contributions of the token (down; combine counting)
 };
 
 template <int TOK>
@@ -588,6 +590,14 @@ __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a,
                 tb.mrow[j] = row0 + jv;
                 tb.slot[j] = sl;
                 tb.w[j] = (sh || gu) ? 0.0f : __ldcg(a.wts + sl);
+            }
+            __syncwarp();
+            // values the epilogue's tail would otherwise fetch from L2 on its critical path
+            if (C::kMinD2 && gu) {
+                const int ncol = a.all_tok ? T : it.n, xrow0 = a.all_tok ? 0 : row0;
+                for (int c = lane; c < ncol; c += 32) tb.xi[c] = __ldcg(a.xinv + (size_t)(xrow0 + c) * 4);
+            } else if (!gu && !a.ep_ranks) {
+                for (int j = lane; j < it.n; j += 32) tb.ex[j] = __ldcg(a.expect + tb.tok[j]);
             }
             bool ok = true;
             if (!gu) {  // the token tile's SwiGLU outputs: every gate/up tile of this sub-job has finished
@@ -950,10 +960,9 @@ __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a,
             float *sv = reinterpret_cast<float *>(smem + kOffV);
             const bool cols_tok = C::kMinD2 && gu && by_tok;  // gate/up planes indexed by token
             if (C::kMinD2 && gu) {
-                const int xrow0 = by_tok ? 0 : (it.expert < 0 ? T * kTop + it.tok0 : it.first);
 #pragma unroll
                 for (int c = 0; c < (C::kMinD2 ? kTok : 1); c++)
-                    if (c < ncol) sv[(half * kTok + c) * kTcRows + r] = acc2[c] * __ldcg(a.xinv + (size_t)(xrow0 + c) * 4);
+                    if (c < ncol) sv[(half * kTok + c) * kTcRows + r] = acc2[c] * tb.xi[c];
             } else {
 #pragma unroll
             for (int cb = 0; cb < kHalf / 8; cb++) {
@@ -1002,13 +1011,16 @@ __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a,
                 bar_named(3, 256);
                 finish = s_last != 0;
                 if (finish) {
-#pragma unroll 1
+#pragma unroll 4
                     for (int j = et >> 7; j < it.n; j += 2) {
                         const float *pp = a.gu_part + (size_t)tb.mrow[j] * kMaxParts * F2 + it.mt * kTcRows + rr;
                         float g = 0.0f, u = 0.0f;
-                        for (int q = 0; q < it.np; q++) {
-                            g += __ldcg(pp + q * F2);
-                            u += __ldcg(pp + q * F2 + F);
+#pragma unroll
+                        for (int q = 0; q < kMaxParts; q++) {
+                            if (q < it.np) {
+                                g += __ldcg(pp + q * F2);
+                                u += __ldcg(pp + q * F2 + F);
+                            }
                         }
                         const int cj = cols_tok ? tb.tok[j] : j;
                         sv[cj * kTcRows + rr] = g;
@@ -1105,7 +1117,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a,
                 if (et < it.n) {
                     const int t = tb.tok[et];
                     int *cnt = a.tilecnt + (size_t)t * dn_mt + it.mt;
-                    const int expect = __ldcg(a.expect + t) & 0xffff;
+                    const int expect = tb.ex[et] & 0xffff;
                     __threadfence();
                     if (atomicAdd(cnt, 1) == expect - 1) {
                         *cnt = 0;
