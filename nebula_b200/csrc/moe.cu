@@ -931,7 +931,11 @@ int run_experts(float *out, const float *x, const int *ids, const float *wts, in
         t.mid16 = reinterpret_cast<__half *>(base + L.mid16);
         t.midinv = reinterpret_cast<float *>(base + L.midinv);
         t.msum = reinterpret_cast<float *>(base + L.msum);
-        t.slots = slots, t.shout = shared, t.out = out;
+        // small batches combine in the expert kernel (last contribution per row tile);
+        // large ones store the weighted rows and reduce them in a combine kernel after
+        // it, which keeps the per-token fences and counts out of the down tiles' tails
+        const bool fused = t.all_tok || ep;
+        t.slots = slots, t.shout = shared, t.out = fused ? out : nullptr;
         DecCtr *ctr = reinterpret_cast<DecCtr *>(base + kHdrBytes);
         t.queue = &ctr->tc_queue, t.tc_ticket = &ctr->tc_ticket;
         t.gu_done = reinterpret_cast<int *>(base + L.gudone);
@@ -949,7 +953,7 @@ int run_experts(float *out, const float *x, const int *ids, const float *wts, in
             Span sp(kPlan, st);
             tc_plan_kernel<<<1, 1024, 0, st>>>(pl, ids, T, H, has_shared ? 1 : 0, const_cast<SubJob *>(t.sub),
                                                const_cast<int *>(t.n_sub), const_cast<int *>(t.expect), t.gu_done,
-                                               t.tilecnt, ep ? nullptr : out, ep ? ep->local : nullptr, t.sh_t0,
+                                               t.tilecnt, (ep || !fused) ? nullptr : out, ep ? ep->local : nullptr, t.sh_t0,
                                                t.sh_t1);
             if (int rc = cudaGetLastError()) return rc;
             const int rc = t.all_tok ? tc_prep_launch(x, T, H, const_cast<__half *>(t.x16), const_cast<float *>(t.xinv),
@@ -959,8 +963,17 @@ int run_experts(float *out, const float *x, const int *ids, const float *wts, in
                                                            const_cast<float *>(t.xsum), st);
             if (rc) return rc;
         }
-        Span sp(kExpertsFused, st);
-        return tc_launch(t, maps, st, false, kTcTok);
+        {
+            Span sp(kExpertsFused, st);
+            if (int rc = tc_launch(t, maps, st, false, kTcTok)) return rc;
+        }
+        if (!fused) {
+            Span sp(kCombine, st);
+            combine_kernel<<<dim3((H / 4 + 127) / 128, T), 128, 0, st>>>(out, slots, ids, wts, pl.bad,
+                                                                        has_shared ? shared : nullptr, sgate,
+                                                                        sgate_stride, T, H);
+        }
+        return cudaGetLastError();
     }
 
     GateUpArgs ga{x, T, H, F, static_cast<const unsigned char *>(gate), static_cast<const unsigned char *>(up),

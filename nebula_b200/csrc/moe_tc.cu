@@ -990,7 +990,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a,
                 // this K part's partial sums; the last part of the tile adds them up in
                 // part order and finishes it
                 const size_t F2 = 2 * (size_t)F;
-#pragma unroll 1
+#pragma unroll 4
                 for (int j = et >> 7; j < it.n; j += 2) {
                     const int cj = cols_tok ? tb.tok[j] : j;
                     float *pp = a.gu_part + ((size_t)tb.mrow[j] * kMaxParts + it.kq) * F2 + it.mt * kTcRows + rr;
@@ -1069,7 +1069,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a,
                 }
                 bar_named(3, 256);
                 // fp16 hi/lo split of v*s for the down tiles
-#pragma unroll 1
+#pragma unroll 4
                 for (int j = et >> 7; j < it.n; j += 2) {
                     const float v = sv[(cols_tok ? tb.tok[j] : j) * kTcRows + rr] * s_scale[j];
                     const __half hi = __float2half_rn(v);
@@ -1087,7 +1087,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a,
                 if (a.ep_ranks) {
                     // every rank's buffers for this call's parity; the combine kernel reduces
                     const int par = __ldcg(a.ep_epoch) & 1;
-#pragma unroll 1
+#pragma unroll 4
                     for (int j = et >> 7; j < it.n; j += 2) {
                         const float y = sv[j * kTcRows + rr];
                         const size_t o = it.expert < 0 ? ((size_t)par * T + tb.tok[j]) * H + row
@@ -1104,11 +1104,16 @@ __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a,
                     if (lane == 0) arrive(&bars.item_empty[slot]);
                     continue;
                 }
-#pragma unroll 1
+#pragma unroll 4
                 for (int j = et >> 7; j < it.n; j += 2) {
                     const float y = sv[j * kTcRows + rr];
                     if (it.expert < 0) a.shout[(size_t)tb.tok[j] * H + row] = y;
                     else a.slots[(size_t)tb.slot[j] * H + row] = y * tb.w[j];
+                }
+                if (!a.out) {  // large batches: a combine kernel after this one reduces the rows
+                    __syncwarp();
+                    if (lane == 0) arrive(&bars.item_empty[slot]);
+                    continue;
                 }
                 if (et == 0) s_ncombine = 0;
                 bar_named(3, 256);

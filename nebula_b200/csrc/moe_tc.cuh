@@ -44,7 +44,7 @@ struct TcArgs {
     float *msum;           // [rows][F/32]: 32-value group sums of v
     float *slots;          // [T*10][H]
     float *shout;          // [T][H]
-    float *out;            // [T][H]
+    float *out;            // [T][H]; null: down tiles only store slot/shared rows (combined by a later kernel)
     int *queue;            // zero between calls (reset by the kernel's last CTA)
     int *tc_ticket;        // zero between calls
     int *gu_done;          // [n_sub] finished gate/up tiles, zeroed by the planner
