@@ -48,45 +48,69 @@ __global__ void __launch_bounds__(kRowsPerCta * 32) matmul_kernel(float *out, co
 // chunks of the rows and token vectors staged in shared memory, then the same
 // 16/8/4/2/1 tree: bitwise the order of one warp per row above.
 constexpr int kTR = 16, kTT = 32, kTK = 256, kTThreads = 256;
+constexpr int kTSmem = 2 * (kTR + kTT) * kTK * 4;  // two stages of row and token chunks
+__device__ __forceinline__ void cp_async16(void *dst, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+// The chunks are staged with cp.async into two alternating buffers, so the
+// next chunk's copies overlap this chunk's multiply-adds.
 __global__ void __launch_bounds__(kTThreads) matmul_f32_tiled_kernel(float *out, const float *w, int rows, int cols,
                                                                      const float *x, int nt) {
-    __shared__ __align__(16) float ws[kTR][kTK];
-    __shared__ __align__(16) float xs[kTT][kTK];
+    extern __shared__ __align__(16) float tsm[];
+    float(*ws)[kTR][kTK] = reinterpret_cast<float(*)[kTR][kTK]>(tsm);
+    float(*xs)[kTT][kTK] = reinterpret_cast<float(*)[kTT][kTK]>(tsm + 2 * kTR * kTK);
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int row0 = blockIdx.x * kTR, tok0 = blockIdx.y * kTT;
     const int wr = (warp >> 2) * 8, wt = (warp & 3) * 8;  // this warp's rows and tokens within the tile
+    auto stage = [&](int b, int kc) {
+        const int kn = min(kTK, cols - kc);  // a multiple of 32
+        for (int i = tid; i < kTR * (kTK / 4); i += kTThreads) {
+            const int r = i / (kTK / 4), c = (i % (kTK / 4)) * 4;
+            float *dst = &ws[b][r][c];
+            if (row0 + r < rows && c < kn) cp_async16(dst, w + (size_t)(row0 + r) * cols + kc + c);
+            else *reinterpret_cast<float4 *>(dst) = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        }
+        for (int i = tid; i < kTT * (kTK / 4); i += kTThreads) {
+            const int t = i / (kTK / 4), c = (i % (kTK / 4)) * 4;
+            float *dst = &xs[b][t][c];
+            if (tok0 + t < nt && c < kn) cp_async16(dst, x + (size_t)(tok0 + t) * cols + kc + c);
+            else *reinterpret_cast<float4 *>(dst) = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        }
+        cp_async_commit();
+    };
     float acc[8][8];
 #pragma unroll
     for (int r = 0; r < 8; r++)
 #pragma unroll
         for (int t = 0; t < 8; t++) acc[r][t] = 0.0f;
-    for (int kc = 0; kc < cols; kc += kTK) {
-        const int kn = min(kTK, cols - kc);  // a multiple of 32
-        __syncthreads();
-        for (int i = tid; i < kTR * (kTK / 4); i += kTThreads) {
-            const int r = i / (kTK / 4), c = (i % (kTK / 4)) * 4;
-            float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-            if (row0 + r < rows && c < kn) v = __ldg(reinterpret_cast<const float4 *>(w + (size_t)(row0 + r) * cols + kc + c));
-            *reinterpret_cast<float4 *>(&ws[r][c]) = v;
-        }
-        for (int i = tid; i < kTT * (kTK / 4); i += kTThreads) {
-            const int t = i / (kTK / 4), c = (i % (kTK / 4)) * 4;
-            float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-            if (tok0 + t < nt && c < kn) v = __ldg(reinterpret_cast<const float4 *>(x + (size_t)(tok0 + t) * cols + kc + c));
-            *reinterpret_cast<float4 *>(&xs[t][c]) = v;
+    stage(0, 0);
+    int b = 0;
+    for (int kc = 0; kc < cols; kc += kTK, b ^= 1) {
+        const int kn = min(kTK, cols - kc);
+        if (kc + kTK < cols) {
+            stage(b ^ 1, kc + kTK);
+            cp_async_wait<1>();
+        } else {
+            cp_async_wait<0>();
         }
         __syncthreads();
         for (int k = lane; k < kn; k += 32) {
             float wv[8], xv[8];
 #pragma unroll
-            for (int r = 0; r < 8; r++) wv[r] = ws[wr + r][k];
+            for (int r = 0; r < 8; r++) wv[r] = ws[b][wr + r][k];
 #pragma unroll
-            for (int t = 0; t < 8; t++) xv[t] = xs[wt + t][k];
+            for (int t = 0; t < 8; t++) xv[t] = xs[b][wt + t][k];
 #pragma unroll
             for (int r = 0; r < 8; r++)
 #pragma unroll
                 for (int t = 0; t < 8; t++) acc[r][t] = __fmaf_rn(wv[r], xv[t], acc[r][t]);
         }
+        __syncthreads();  // buffer b is restaged two chunks later
     }
 #pragma unroll
     for (int r = 0; r < 8; r++)
@@ -141,7 +165,9 @@ int launch_matmul(float *o, const void *w, int type, int rows, int cols, const f
         return cudaErrorInvalidValue;
     if (type == 0 && nt >= 64 && cols % 32 == 0 && !(reinterpret_cast<uintptr_t>(w) & 15) &&
         !(reinterpret_cast<uintptr_t>(x) & 15)) {  // fp32 rows against a large batch: tiled
-        matmul_f32_tiled_kernel<<<dim3((rows + kTR - 1) / kTR, (nt + kTT - 1) / kTT), kTThreads, 0, st>>>(
+        if (int rc = cudaFuncSetAttribute(matmul_f32_tiled_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kTSmem))
+            return rc;
+        matmul_f32_tiled_kernel<<<dim3((rows + kTR - 1) / kTR, (nt + kTT - 1) / kTT), kTThreads, kTSmem, st>>>(
             o, static_cast<const float *>(w), rows, cols, x, nt);
         return cudaGetLastError();
     }
