@@ -42,13 +42,15 @@ __global__ void __launch_bounds__(kRowsPerCta * 32) matmul_kernel(float *out, co
     }
 }
 
-// fp32 weights, large batches: a CTA computes 16 rows x 32 tokens. Lane j of
+// fp32 weights, large batches: a CTA computes TR rows x TT tokens (32 x 32, or
+// 8 x 16 for a handful of rows such as the shared-expert gate). Lane j of
 // every warp holds the partial sums over k = j (mod 32) of an 8-row x 8-token
 // tile, accumulated in increasing k with fused multiply-adds from 256-column
 // chunks of the rows and token vectors staged in shared memory, then the same
 // 16/8/4/2/1 tree: bitwise the order of one warp per row above.
-constexpr int kTR = 16, kTT = 32, kTK = 256, kTThreads = 256;
-constexpr int kTSmem = 2 * (kTR + kTT) * kTK * 4;  // two stages of row and token chunks
+constexpr int kTK = 256;
+template <int TR, int TT>
+constexpr int tiled_smem() { return 2 * (TR + TT) * kTK * 4; }  // two stages of row and token chunks
 __device__ __forceinline__ void cp_async16(void *dst, const void *src) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src)
                  : "memory");
@@ -59,14 +61,16 @@ __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_gr
 
 // The chunks are staged with cp.async into two alternating buffers, so the
 // next chunk's copies overlap this chunk's multiply-adds.
-__global__ void __launch_bounds__(kTThreads) matmul_f32_tiled_kernel(float *out, const float *w, int rows, int cols,
-                                                                     const float *x, int nt) {
+template <int kTR, int kTT>
+__global__ void __launch_bounds__(kTR * kTT / 2) matmul_f32_tiled_kernel(float *out, const float *w, int rows, int cols,
+                                                                         const float *x, int nt) {
+    constexpr int kTThreads = kTR * kTT / 2;  // one warp per 8 x 8 tile
     extern __shared__ __align__(16) float tsm[];
     float(*ws)[kTR][kTK] = reinterpret_cast<float(*)[kTR][kTK]>(tsm);
     float(*xs)[kTT][kTK] = reinterpret_cast<float(*)[kTT][kTK]>(tsm + 2 * kTR * kTK);
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int row0 = blockIdx.x * kTR, tok0 = blockIdx.y * kTT;
-    const int wr = (warp >> 2) * 8, wt = (warp & 3) * 8;  // this warp's rows and tokens within the tile
+    const int wr = (warp / (kTT / 8)) * 8, wt = (warp % (kTT / 8)) * 8;  // this warp's rows and tokens
     auto stage = [&](int b, int kc) {
         const int kn = min(kTK, cols - kc);  // a multiple of 32
         for (int i = tid; i < kTR * (kTK / 4); i += kTThreads) {
@@ -122,6 +126,14 @@ __global__ void __launch_bounds__(kTThreads) matmul_f32_tiled_kernel(float *out,
         }
 }
 
+template <int TR, int TT>
+int launch_tiled(float *o, const float *w, int rows, int cols, const float *x, int nt, cudaStream_t st) {
+    auto k = matmul_f32_tiled_kernel<TR, TT>;
+    if (int rc = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, tiled_smem<TR, TT>())) return rc;
+    k<<<dim3((rows + TR - 1) / TR, (nt + TT - 1) / TT), TR * TT / 2, tiled_smem<TR, TT>(), st>>>(o, w, rows, cols, x, nt);
+    return cudaGetLastError();
+}
+
 __global__ void gather_kernel(float *out, const unsigned char *w, int type, int n, size_t stride, int row) {
     int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i < n) out[i] = decode_at(w + (size_t)row * stride, type, i);
@@ -165,10 +177,9 @@ int launch_matmul(float *o, const void *w, int type, int rows, int cols, const f
         return cudaErrorInvalidValue;
     if (type == 0 && nt >= 64 && cols % 32 == 0 && !(reinterpret_cast<uintptr_t>(w) & 15) &&
         !(reinterpret_cast<uintptr_t>(x) & 15)) {  // fp32 rows against a large batch: tiled
-        if (int rc = cudaFuncSetAttribute(matmul_f32_tiled_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kTSmem))
-            return rc;
-        matmul_f32_tiled_kernel<<<dim3((rows + kTR - 1) / kTR, (nt + kTT - 1) / kTT), kTThreads, kTSmem, st>>>(
-            o, static_cast<const float *>(w), rows, cols, x, nt);
+        const float *wf = static_cast<const float *>(w);
+        if (rows >= 32) return launch_tiled<32, 32>(o, wf, rows, cols, x, nt, st);
+        return launch_tiled<8, 16>(o, wf, rows, cols, x, nt, st);
         return cudaGetLastError();
     }
     dim3 grid((rows + kRowsPerCta - 1) / kRowsPerCta, (nt + kTokTile - 1) / kTokTile);

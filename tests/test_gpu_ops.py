@@ -77,6 +77,19 @@ def test_router_gemv_bitwise_at_model_shape(L, ref2048, nt):
     np.testing.assert_array_equal(out.get(), ref2048.matmul(router.view(np.uint8), 0, 512, 2048, x))
 
 
+@pytest.mark.parametrize("rows,nt", ((1, 2048), (1, 100), (48, 100), (40, 77)))
+def test_tiled_gemv_ragged_shapes_bitwise(L, ref2048, rows, nt):
+    """The tiled fp32 kernel on a shared-gate row (8 x 16 tiles) and on row and
+    token counts that leave partial tiles (32 x 32 tiles), bitwise qc_matmul."""
+    rng = np.random.default_rng(rows * 1000 + nt)
+    w = rng.normal(0, 0.02, (rows, 2048)).astype(np.float32)
+    x = rng.normal(0, 1, (nt, 2048)).astype(np.float32)
+    dw, dx = L.Device(w), L.Device(x)
+    out = L.Device.empty((nt, rows), np.float32)
+    L.call("matmul", out.p, dw.p, 0, rows, 2048, dx.p, nt)
+    np.testing.assert_array_equal(out.get(), ref2048.matmul(w.view(np.uint8), 0, rows, 2048, x))
+
+
 def test_route_matches_restatement(L, restate):
     rng = np.random.default_rng(812603)
     nt = 2048
