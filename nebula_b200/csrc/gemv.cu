@@ -87,11 +87,13 @@ __global__ void __launch_bounds__(kTR * kTT / 2) matmul_f32_tiled_kernel(float *
         }
         cp_async_commit();
     };
-    float acc[8][8];
+    // acc[r][p] holds tokens 2p and 2p+1 of row r: paired fused multiply-adds,
+    // each half the same rounding as a scalar one
+    float2 acc[8][4];
 #pragma unroll
     for (int r = 0; r < 8; r++)
 #pragma unroll
-        for (int t = 0; t < 8; t++) acc[r][t] = 0.0f;
+        for (int p = 0; p < 4; p++) acc[r][p] = make_float2(0.0f, 0.0f);
     stage(0, 0);
     int b = 0;
     for (int kc = 0; kc < cols; kc += kTK, b ^= 1) {
@@ -104,15 +106,18 @@ __global__ void __launch_bounds__(kTR * kTT / 2) matmul_f32_tiled_kernel(float *
         }
         __syncthreads();
         for (int k = lane; k < kn; k += 32) {
-            float wv[8], xv[8];
+            float wv[8];
+            float2 xv[4];
 #pragma unroll
             for (int r = 0; r < 8; r++) wv[r] = ws[b][wr + r][k];
 #pragma unroll
-            for (int t = 0; t < 8; t++) xv[t] = xs[b][wt + t][k];
+            for (int p = 0; p < 4; p++) xv[p] = make_float2(xs[b][wt + 2 * p][k], xs[b][wt + 2 * p + 1][k]);
 #pragma unroll
-            for (int r = 0; r < 8; r++)
+            for (int r = 0; r < 8; r++) {
+                const float2 w2 = make_float2(wv[r], wv[r]);
 #pragma unroll
-                for (int t = 0; t < 8; t++) acc[r][t] = __fmaf_rn(wv[r], xv[t], acc[r][t]);
+                for (int p = 0; p < 4; p++) acc[r][p] = __ffma2_rn(w2, xv[p], acc[r][p]);
+            }
         }
         __syncthreads();  // buffer b is restaged two chunks later
     }
@@ -120,7 +125,7 @@ __global__ void __launch_bounds__(kTR * kTT / 2) matmul_f32_tiled_kernel(float *
     for (int r = 0; r < 8; r++)
 #pragma unroll
         for (int t = 0; t < 8; t++) {
-            const float s = lane_tree(acc[r][t]);
+            const float s = lane_tree((t & 1) ? acc[r][t >> 1].y : acc[r][t >> 1].x);
             const int row = row0 + wr + r, tok = tok0 + wt + t;
             if (lane == 0 && row < rows && tok < nt) out[(size_t)tok * rows + row] = s;
         }

@@ -158,6 +158,7 @@ __global__ void __launch_bounds__(kK1Threads) dec_router_kernel(DecArgs a) {
 #pragma unroll
                 for (int i = 0; i < kTpw; i++) acc[i] = 0.0f;
                 const float *w = wr + (size_t)r * H;
+#pragma unroll 4
                 for (int k = lane; k < H; k += 32) {
                     const float wv = w[k];
 #pragma unroll
