@@ -1034,7 +1034,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a,
             } else if (gu) {
                 // per token (one warp each): the four 32-row group sums and a power-of-two
                 // scale from the tile's max |v|
-#pragma unroll 1
+#pragma unroll 3
                 for (int j = ew; j < it.n; j += kEpiWarps) {
                     // SwiGLU of the token's 128 rows, kept in plane 0 for the split below
                     const int cj = cols_tok ? tb.tok[j] : j;
