@@ -96,11 +96,14 @@ constexpr int kTP = 4;               // tokens per pass
 constexpr int kGateUpRows = 16;      // rows of gate (and of up) per CTA
 constexpr int kDownRows = 64;        // rows of down per CTA
 constexpr int kPlanChunk = 512;      // tokens per bitmap chunk in the plan kernel
+constexpr int kPC = 128;             // tokens per CTA of the multi-CTA plan (large batches)
+constexpr int kPlanMultiMin = 256;   // batches from this size plan with several CTAs
 
 // ---------------------------------------------------------------- workspace
 struct Layout {
     size_t hdr, counts, off, used, pairs, bad, logits, ids, wts, mid, slots, shared;
-    size_t x16, xinv, xsum, sub, nsub, mid16, midinv, msum, gudone, tilecnt, expect, total;  // tensor-core path
+    size_t x16, xinv, xsum, sub, nsub, mid16, midinv, msum, gudone, tilecnt, expect;  // tensor-core path
+    size_t pcnt, total;  // multi-CTA plan: per chunk of kPC tokens, per-expert counts then offsets, + invalid
 };
 
 inline int max_subjobs(int T) { return (T + kTcTok - 1) / kTcTok + kExperts + (T * kTop + kTcTok - 1) / kTcTok; }
@@ -140,6 +143,7 @@ Layout layout(int T, int H, int F) {
     L.gudone = take(sizeof(int) * (size_t)max_subjobs(T));
     L.tilecnt = take(sizeof(int) * (size_t)T * (H / kTcRows));
     L.expect = take(sizeof(int) * (size_t)T);
+    L.pcnt = take(sizeof(int) * (size_t)((T + kPC - 1) / kPC) * (kExperts + 1));
     L.total = p;
     return L;
 }
@@ -289,6 +293,151 @@ __global__ void __launch_bounds__(1024) plan_kernel(const int *ids, const float 
             int total = 0;
             for (int w2 = 0; w2 < W; w2++) total += __popc(bm[e * W + w2]);
             run[e] += total;
+        }
+    }
+}
+
+// Multi-CTA plan for large batches: the same validation, offsets and pair
+// order (ascending tokens within each expert) as plan_kernel, in three steps.
+// Validation follows qc_moe (qwen/cpu.c:241-246); e_k gets -1 for an omitted route.
+__device__ __forceinline__ bool plan_validate(const int *ids, const float *wts, int t, int (&e_k)[kTop]) {
+    bool ok = true;
+#pragma unroll
+    for (int k = 0; k < kTop; k++) {
+        const int e = ids[t * kTop + k];
+        const float w = wts[t * kTop + k];
+        e_k[k] = e;
+        if (e <= -2 && e >= -kExperts - 1 && w == 0.0f) {
+            e_k[k] = -1;
+            continue;
+        }
+        if (e < 0 || e >= kExperts || !(w >= 0.0f) || isinf(w)) ok = false;
+#pragma unroll
+        for (int j = 0; j < k; j++)
+            if (ids[t * kTop + j] == e) ok = false;
+    }
+    return ok;
+}
+
+// Step 1 (CTA c: tokens [c*kPC, (c+1)*kPC)): validation, and the chunk's count
+// per expert and of invalid tokens into pcnt[c][0..512].
+__global__ void __launch_bounds__(512) plan_count_kernel(const int *ids, const float *wts, int nt, Plan pl, int *pcnt) {
+    constexpr int W = kPC / 32;
+    __shared__ unsigned bm[kExperts * W];
+    __shared__ int s_inv;
+    const int tid = threadIdx.x, c0 = blockIdx.x * kPC, c1 = min(nt, c0 + kPC);
+    for (int i = tid; i < kExperts * W; i += blockDim.x) bm[i] = 0;
+    if (tid == 0) s_inv = 0;
+    __syncthreads();
+    for (int t = c0 + tid; t < c1; t += blockDim.x) {
+        int e_k[kTop];
+        const bool ok = plan_validate(ids, wts, t, e_k);
+        pl.bad[t] = ok ? 0 : 1;
+        if (ok) {
+#pragma unroll
+            for (int k = 0; k < kTop; k++)
+                if (e_k[k] >= 0) atomicOr(&bm[e_k[k] * W + (t - c0) / 32], 1u << ((t - c0) & 31));
+        } else {
+            atomicAdd(&s_inv, 1);
+        }
+    }
+    __syncthreads();
+    int *row = pcnt + (size_t)blockIdx.x * (kExperts + 1);
+    for (int e = tid; e < kExperts; e += blockDim.x) {
+        int n = 0;
+#pragma unroll
+        for (int w = 0; w < W; w++) n += __popc(bm[e * W + w]);
+        row[e] = n;
+    }
+    if (tid == 0) row[kExperts] = s_inv;
+}
+
+// Step 2 (one CTA, thread e = expert): totals, offsets, the used-expert list and
+// the header; pcnt[c][e] becomes the first pair position of chunk c's tokens of e.
+__global__ void __launch_bounds__(kExperts) plan_scan_kernel(int nchunks, Plan pl, int *pcnt) {
+    __shared__ int warp_tot[32];
+    const int e = threadIdx.x, lane = e & 31, warp = e >> 5;
+    int c = 0;
+    for (int ch = 0; ch < nchunks; ch++) {
+        int *v = pcnt + (size_t)ch * (kExperts + 1) + e;
+        const int n = *v;
+        *v = c;
+        c += n;
+    }
+    int incl = c;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+        const int v = __shfl_up_sync(0xffffffffu, incl, d);
+        if (lane >= d) incl += v;
+    }
+    if (lane == 31) warp_tot[warp] = incl;
+    __syncthreads();
+    if (e < 32) {
+        const int v = e < kExperts / 32 ? warp_tot[e] : 0;
+        int s2 = v;
+#pragma unroll
+        for (int d = 1; d < 32; d <<= 1) {
+            const int o = __shfl_up_sync(0xffffffffu, s2, d);
+            if (e >= d) s2 += o;
+        }
+        warp_tot[e] = s2 - v;
+    }
+    __syncthreads();
+    const int excl = warp_tot[warp] + incl - c;
+    pl.off[e] = excl;
+    pl.counts[e] = c;
+    if (e == kExperts - 1) {
+        pl.off[kExperts] = excl + c;
+        pl.hdr->n_pairs = excl + c;
+    }
+    for (int ch = 0; ch < nchunks; ch++) pcnt[(size_t)ch * (kExperts + 1) + e] += excl;
+    __syncthreads();
+    {
+        const unsigned m = __ballot_sync(0xffffffffu, c > 0);
+        if (lane == 0) warp_tot[warp] = __popc(m);
+    }
+    __syncthreads();
+    {
+        const unsigned m = __ballot_sync(0xffffffffu, c > 0);
+        int before = __popc(m & ((1u << lane) - 1));
+        for (int w = 0; w < warp; w++) before += warp_tot[w];
+        if (c > 0) pl.used[before] = e;
+        if (e == kExperts - 1) pl.hdr->n_used = before + (c > 0);
+    }
+    if (e == 0) {
+        int inv = 0;
+        for (int ch = 0; ch < nchunks; ch++) inv += pcnt[(size_t)ch * (kExperts + 1) + kExperts];
+        pl.hdr->invalid_tokens = inv;
+    }
+}
+
+// Step 3 (CTA c): each valid pair's position is its chunk's start for the expert
+// plus the chunk's earlier tokens of that expert (set bits below it).
+__global__ void __launch_bounds__(512) plan_place_kernel(const int *ids, int nt, Plan pl, const int *pcnt) {
+    constexpr int W = kPC / 32;
+    __shared__ unsigned bm[kExperts * W];
+    const int tid = threadIdx.x, c0 = blockIdx.x * kPC, c1 = min(nt, c0 + kPC);
+    for (int i = tid; i < kExperts * W; i += blockDim.x) bm[i] = 0;
+    __syncthreads();
+    for (int t = c0 + tid; t < c1; t += blockDim.x) {
+        if (pl.bad[t]) continue;
+        for (int k = 0; k < kTop; k++) {
+            const int e = ids[t * kTop + k];
+            if (e >= 0) atomicOr(&bm[e * W + (t - c0) / 32], 1u << ((t - c0) & 31));
+        }
+    }
+    __syncthreads();
+    const int *start = pcnt + (size_t)blockIdx.x * (kExperts + 1);
+    for (int t = c0 + tid; t < c1; t += blockDim.x) {
+        if (pl.bad[t]) continue;
+        const int wd = (t - c0) / 32;
+        const unsigned below = (1u << ((t - c0) & 31)) - 1u;
+        for (int k = 0; k < kTop; k++) {
+            const int e = ids[t * kTop + k];
+            if (e < 0) continue;
+            int pos = start[e] + __popc(bm[e * W + wd] & below);
+            for (int w2 = 0; w2 < wd; w2++) pos += __popc(bm[e * W + w2]);
+            pl.pairs[pos] = t * kTop + k;
         }
     }
 }
@@ -904,7 +1053,15 @@ int run_experts(float *out, const float *x, const int *ids, const float *wts, in
 
     {
         Span sp(kPlan, st);
-        plan_kernel<<<1, 1024, 0, st>>>(ids, wts, T, pl);
+        if (T >= kPlanMultiMin) {
+            const int nch = (T + kPC - 1) / kPC;
+            int *pcnt = reinterpret_cast<int *>(base + L.pcnt);
+            plan_count_kernel<<<nch, 512, 0, st>>>(ids, wts, T, pl, pcnt);
+            plan_scan_kernel<<<1, kExperts, 0, st>>>(nch, pl, pcnt);
+            plan_place_kernel<<<nch, 512, 0, st>>>(ids, T, pl, pcnt);
+        } else {
+            plan_kernel<<<1, 1024, 0, st>>>(ids, wts, T, pl);
+        }
     }
     if (int rc = cudaGetLastError()) return rc;
     if (tc_supported(H, F, gt, dt)) {

@@ -165,6 +165,30 @@ def test_invalid_and_omitted_routes(L, ref2048, q4k_2048):
     assert inv == 4 and sel == 5 * 10 - 2
 
 
+def test_invalid_and_omitted_routes_large_batch(L, ref2048, q4k_2048):
+    """A batch planned by several CTAs (chunks of 128 tokens, the last one
+    ragged), with invalid and omitted routes in different chunks."""
+    rng = np.random.default_rng(17)
+    T = 300
+    x = rng.normal(0, 1, (T, 2048)).astype(np.float32)
+    ids, w = random_routes(rng, T)
+    for t, k in ((0, 9), (200, 3), (299, 0)):
+        ids[t, k], w[t, k] = -ids[t, k] - 2, 0.0
+    bad, bad_w = ids.copy(), w.copy()
+    bad[1, :] = -1
+    bad[130, 4] = bad[130, 3]
+    bad_w[257, 0] = np.nan
+    bad_w[298, 1] = -0.1
+    out, ws = q4k_2048.routed(x, bad, bad_w)
+    good = [t for t in range(T) if t not in (1, 130, 257, 298)]
+    expected = oracle_routed(ref2048, q4k_2048, x[good], ids[good], w[good])
+    assert_parity(out[good], expected, "large batch: valid rows next to invalid ones")
+    assert np.isnan(out[[1, 130, 257, 298]]).all()
+    inv, sel, used = L.status(ws)
+    assert inv == 4 and sel == len(good) * 10 - 3
+    assert used == len(np.unique(ids[good][ids[good] >= 0]))
+
+
 def test_workspace_reuse_across_paths(L, ref2048, q4k_2048):
     """One zeroed workspace serves many calls: decode-path calls (T <= 17) leave
     their counters at zero, and large-batch calls in between do not disturb them."""
