@@ -176,9 +176,12 @@ int qg_moe_layer(float *out, int *ids_out, float *weights_out, const float *x, i
  * every rank; a rank that stops makes the others' combines time out (error
  * bit 8 in qg_moe_status) instead of hanging. Q4_K only.
  * Large batches (tokens > 32): rank r owns tokens [r*B, (r+1)*B) with
- * B = ceil(tokens / ranks); each rank computes the shared expert for its own
- * tokens (shared_rank is not used), stores each weighted row only into the
- * owning rank's workspace, and writes only its own rows of `out`. */
+ * B = ceil(tokens / ranks); each rank computes the router logits and top-10
+ * of its own tokens and sends their ids and weights to every rank (ids_out
+ * and weights_out receive all tokens on every rank), computes the shared
+ * expert for its own tokens (shared_rank is not used), stores each weighted
+ * row only into the owning rank's workspace, and writes only its own rows of
+ * `out`. */
 int qg_ep_workspace_bytes(int tokens, int hidden, int ffn, size_t *bytes);
 int qg_ep_ipc_handle(void *workspace, void *handle);
 int qg_ep_ipc_open(const void *handle, void **ptr);

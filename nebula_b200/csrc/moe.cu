@@ -1337,7 +1337,7 @@ extern "C" int qg_moe_profile_read(int phase, double *total_ms, int *launches) {
 namespace {
 
 struct EpLayout {
-    size_t slots, shout, flags, epoch, total;
+    size_t slots, shout, flags, epoch, rids, rwts, rflags, total;
 };
 
 EpLayout ep_layout(int T, int H, int F) {
@@ -1352,6 +1352,9 @@ EpLayout ep_layout(int T, int H, int F) {
     E.shout = take(sizeof(float) * 2 * (size_t)T * H);         // [2][T][H]
     E.flags = take(sizeof(int) * kMaxRanks);                     // epoch reached by each source rank
     E.epoch = take(sizeof(int) * 2);                             // call epoch, combine ticket
+    E.rids = take(sizeof(int) * (size_t)T * kTop);               // large batches: every rank's routes
+    E.rwts = take(sizeof(float) * (size_t)T * kTop);
+    E.rflags = take(sizeof(int) * kMaxRanks);                    // epoch whose routes each rank has sent
     E.total = p;
     return E;
 }
@@ -1409,6 +1412,62 @@ __global__ void ep_combine_kernel(float *out, const float *slots, const float *s
     }
 }
 
+// Large-batch expert parallelism: each rank routes its own token block and
+// shares the ids and weights. CTA p copies rows [t0, t1) into rank p's route
+// table, then raises this rank's route flag there for this call (system-scope
+// release after a system fence, as for the slot rows).
+struct EpRoutes {
+    int *rids[kMaxRanks];
+    float *rwts[kMaxRanks];
+    int *rflags[kMaxRanks];
+};
+
+__global__ void ep_routes_send_kernel(const int *ids, const float *wts, int t0, int t1, EpRoutes pr, int rank,
+                                      const int *epoch) {
+    const int p = blockIdx.x;
+    int *dids = pr.rids[p];
+    float *dwts = pr.rwts[p];
+    for (int i = t0 * kTop + (int)threadIdx.x; i < t1 * kTop; i += blockDim.x) {
+        dids[i] = ids[i];
+        dwts[i] = wts[i];
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence_system();
+        const int e = __ldcg(epoch) + 1;
+        asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(pr.rflags[p] + rank), "r"(e) : "memory");
+    }
+}
+
+// Waits (bounded: error bit 8, and ids -1 so every token is reported invalid)
+// until every rank's routes of this call are in this rank's table, then copies
+// the whole table to ids / wts.
+__global__ void ep_routes_recv_kernel(int *ids, float *wts, const int *rids, const float *rwts, int T, int ranks,
+                                      const int *rflags, const int *epoch, int *err) {
+    __shared__ int s_ok;
+    if (threadIdx.x == 0) {
+        const int e = __ldcg(epoch);
+        int ok = 1;
+        const uint64_t t0 = global_ns();
+        for (int p = 0; p < ranks && ok; p++)
+            while (ld_acquire_sys(rflags + p) < e + 1) {
+                if (global_ns() - t0 > kWaitLimitNs) {
+                    atomicOr(err, 8);
+                    ok = 0;
+                    break;
+                }
+                __nanosleep(100);
+            }
+        s_ok = ok;
+    }
+    __syncthreads();
+    const bool ok = s_ok != 0;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < T * kTop; i += gridDim.x * blockDim.x) {
+        ids[i] = ok ? __ldcg(rids + i) : -1;
+        wts[i] = ok ? __ldcg(rwts + i) : 0.0f;
+    }
+}
+
 }  // namespace
 
 extern "C" int qg_ep_workspace_bytes(int tokens, int hidden, int ffn, size_t *bytes) {
@@ -1458,10 +1517,12 @@ extern "C" int qg_moe_layer_ep(float *out, int *ids_out, float *weights_out, con
         return cudaErrorInvalidValue;
     cudaStream_t st = launch_stream;
     if (large) {
-        // Large batch: every rank routes all tokens; rank r runs its experts on the
-        // pairs routed to them and the shared expert on its own tokens
-        // [r*block, (r+1)*block), stores each weighted row into the buffers of the
-        // token's rank, and combines its own tokens once every rank has finished.
+        // Large batch: rank r owns tokens [r*block, (r+1)*block). It computes their
+        // router logits and top-10 and sends the ids and weights to every rank, so
+        // each rank holds all routes without repeating the router; it then runs
+        // its experts on the pairs routed to them and the shared expert on its own
+        // tokens, stores each weighted row into the buffers of the token's rank,
+        // and combines its own tokens once every rank has finished.
         const Layout L = layout(tokens, hidden, ffn);
         const EpLayout EL = ep_layout(tokens, hidden, ffn);
         char *b = static_cast<char *>(workspace);
@@ -1469,29 +1530,46 @@ extern "C" int qg_moe_layer_ep(float *out, int *ids_out, float *weights_out, con
         float *sgate = logits + (size_t)tokens * kExperts;
         int *ids = ids_out ? ids_out : reinterpret_cast<int *>(b + L.ids);
         float *wts = weights_out ? weights_out : reinterpret_cast<float *>(b + L.wts);
-        int rc;
-        {
+        const int block = (tokens + ranks - 1) / ranks;
+        const int t0 = std::min(tokens, rank * block), t1 = std::min(tokens, t0 + block), nb = t1 - t0;
+        int rc = 0;
+        if (nb > 0) {
             Span sp(kRouter, st);
-            rc = launch_matmul(logits, router, 0, kExperts, hidden, x, tokens, st);
-            if (!rc && sg) rc = launch_matmul(sgate, s_router, 0, 1, hidden, x, tokens, st);
+            const float *xb = x + (size_t)t0 * hidden;
+            rc = launch_matmul(logits + (size_t)t0 * kExperts, router, 0, kExperts, hidden, xb, nb, st);
+            if (!rc && sg) rc = launch_matmul(sgate + t0, s_router, 0, 1, hidden, xb, nb, st);
         }
         if (rc) return rc;
+        int *epoch = reinterpret_cast<int *>(b + EL.epoch);
         {
             Span sp(kRoute, st);
-            rc = launch_route(ids, wts, logits, logit_bias, tokens, st);
+            if (nb > 0 &&
+                (rc = launch_route(ids + (size_t)t0 * kTop, wts + (size_t)t0 * kTop, logits + (size_t)t0 * kExperts,
+                                   logit_bias, nb, st)))
+                return rc;
+            EpRoutes pr;
+            for (int p = 0; p < ranks; p++) {
+                char *pb = static_cast<char *>(workspaces[p]);
+                pr.rids[p] = reinterpret_cast<int *>(pb + EL.rids);
+                pr.rwts[p] = reinterpret_cast<float *>(pb + EL.rwts);
+                pr.rflags[p] = reinterpret_cast<int *>(pb + EL.rflags);
+            }
+            ep_routes_send_kernel<<<ranks, 256, 0, st>>>(ids, wts, t0, t1, pr, rank, epoch);
+            ep_routes_recv_kernel<<<16, 256, 0, st>>>(ids, wts, pr.rids[rank], pr.rwts[rank], tokens, ranks,
+                                                       pr.rflags[rank], epoch,
+                                                       &reinterpret_cast<Header *>(b + L.hdr)->error);
+            if ((rc = cudaGetLastError())) return rc;
         }
-        if (rc) return rc;
         EpRun ep{};
         ep.local = expert_local, ep.n_local = n_local, ep.ranks = ranks, ep.rank = rank;
-        ep.block = (tokens + ranks - 1) / ranks;
-        ep.t0 = std::min(tokens, rank * ep.block), ep.t1 = std::min(tokens, ep.t0 + ep.block);
+        ep.block = block, ep.t0 = t0, ep.t1 = t1;
         for (int p = 0; p < ranks; p++) {
             char *pb = static_cast<char *>(workspaces[p]);
             ep.slots[p] = reinterpret_cast<float *>(pb + EL.slots);
             ep.shout[p] = reinterpret_cast<float *>(pb + EL.shout);
             ep.flags[p] = reinterpret_cast<int *>(pb + EL.flags);
         }
-        ep.epoch = reinterpret_cast<int *>(b + EL.epoch);
+        ep.epoch = epoch;
         if ((rc = run_experts(out, x, ids, wts, tokens, gate, gt, up, ut, down, dt, sg, sgt, su, sut, sd, sdt, sgate, 1,
                               hidden, ffn, workspace, st, &ep)))
             return rc;

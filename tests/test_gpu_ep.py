@@ -88,7 +88,7 @@ def _worker(rank, world, port, results, T):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("T", (17, 100))
+@pytest.mark.parametrize("T", (17, 100, 2048))
 def test_expert_parallel_matches_single_gpu(T):
     import torch
     world = 2
