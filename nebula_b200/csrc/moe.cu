@@ -110,9 +110,11 @@ inline int max_subjobs(int T) { return (T + kTcTok - 1) / kTcTok + kExperts + (T
 
 inline size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
 
-Layout layout(int T, int H, int F) {
+// Regions from `start`: the status words and decode-path counters (the fixed
+// prefix) come first; expert parallelism also puts its fixed block before start.
+Layout layout(int T, int H, int F, size_t start = kPrefixBytes) {
     Layout L{};
-    size_t p = kPrefixBytes;  // status words and decode-path counters come first
+    size_t p = start;
     auto take = [&](size_t bytes) {
         size_t at = p;
         p = align256(p + bytes);
@@ -1021,6 +1023,7 @@ int launch_down(const DownArgs &a, cudaStream_t st) {
 struct EpRun {
     const int *local;  // [512] each expert's index on this rank, or -1
     int n_local, ranks, rank, block, t0, t1;
+    size_t start;      // offset of the per-call regions in the workspace
     float *slots[kMaxRanks], *shout[kMaxRanks];
     int *flags[kMaxRanks];
     int *epoch;
@@ -1042,7 +1045,7 @@ int run_experts(float *out, const float *x, const int *ids, const float *wts, in
         if (!su || !sd || !sgate || sgt != gt || sut != gt || sdt != dt) return cudaErrorInvalidValue;
         if (!aligned16(sg) || !aligned16(su) || !aligned16(sd)) return cudaErrorInvalidValue;
     }
-    Layout L = layout(T, H, F);
+    Layout L = layout(T, H, F, ep ? ep->start : kPrefixBytes);
     char *base = static_cast<char *>(ws);
     if (!aligned16(base)) return cudaErrorInvalidValue;
     Plan pl = plan_ptrs(ws, L);
@@ -1101,6 +1104,7 @@ int run_experts(float *out, const float *x, const int *ids, const float *wts, in
         t.n_experts = ep ? ep->n_local : kExperts;
         if (ep) {
             t.ep_ranks = ep->ranks, t.ep_rank = ep->rank, t.ep_block = ep->block, t.ep_epoch = ep->epoch;
+            t.ep_cap = 0;  // one set of rows: a peer stores a call's rows only after this rank sent its routes
             for (int r = 0; r < kMaxRanks; r++)
                 t.ep_slots[r] = ep->slots[r], t.ep_shout[r] = ep->shout[r], t.ep_flags[r] = ep->flags[r];
         }
@@ -1171,9 +1175,10 @@ extern "C" int qg_moe_workspace_bytes(int tokens, int hidden, int ffn, size_t *b
 
 namespace {
 // Decode-path arguments over the workspace; ids/wts point at the routing.
-DecArgs dec_args(int T, int H, int F, int gt, int dt, const float *x, float *out, int *ids, float *wts, void *ws) {
+DecArgs dec_args(int T, int H, int F, int gt, int dt, const float *x, float *out, int *ids, float *wts, void *ws,
+                 size_t start = kPrefixBytes) {
     DecArgs a{};
-    DecLayout L = dec_layout(T, H, F);
+    DecLayout L = dec_layout(T, H, F, start);
     char *b = static_cast<char *>(ws);
     a.T = T, a.H = H, a.F = F, a.QG = gt, a.QD = dt;
     a.x = x;
@@ -1332,30 +1337,57 @@ extern "C" int qg_moe_profile_read(int phase, double *total_ms, int *launches) {
 // the shared expert's rows) straight into every rank's workspace over NVLink.
 // Its last CTA then raises its flag in every rank. Each rank's combine kernel
 // waits for all flags of the call (bounded), reduces in router-rank order and
-// advances the call epoch; slot buffers alternate with the epoch's parity, so
-// a rank one layer ahead never overwrites rows a peer is still combining.
+// advances the call epoch.
+//
+// Workspace: everything kept from call to call and everything a peer writes
+// before this rank has finished its previous call sits at offsets that do not
+// depend on the call's token count, so one workspace serves batches of any
+// size up to the one it was sized for, in any order:
+//   fixed prefix (status words, decode counters)
+//   fixed block: flags, epoch, route flags, the route table (8192 tokens), and
+//                the decode batches' slot/shared rows, two sets of 32 tokens
+//                (a rank one call ahead writes the other parity's set, never
+//                rows a peer is still combining)
+//   per-call regions of this rank (dec_layout / layout from the block's end)
+//   large batches: one set of slot/shared rows after those (a peer stores a
+//                call's rows only after every rank has sent that call's routes,
+//                i.e. after this rank's previous combine has finished)
 namespace {
 
-struct EpLayout {
-    size_t slots, shout, flags, epoch, rids, rwts, rflags, total;
+struct EpFixed {
+    size_t flags, epoch, rflags, rids, rwts, dslots, dshout, start;
 };
 
-EpLayout ep_layout(int T, int H, int F) {
-    EpLayout E{};
-    size_t p = align256(T <= kMaxDecodeTokens ? dec_layout(T, H, F).total : layout(T, H, F).total);
+EpFixed ep_fixed(int H) {
+    EpFixed E{};
+    size_t p = kPrefixBytes;
     auto take = [&](size_t bytes) {
         size_t at = p;
         p = align256(p + bytes);
         return at;
     };
-    E.slots = take(sizeof(float) * 2 * (size_t)T * kTop * H);  // [2][T*10][H]
-    E.shout = take(sizeof(float) * 2 * (size_t)T * H);         // [2][T][H]
-    E.flags = take(sizeof(int) * kMaxRanks);                     // epoch reached by each source rank
-    E.epoch = take(sizeof(int) * 2);                             // call epoch, combine ticket
-    E.rids = take(sizeof(int) * (size_t)T * kTop);               // large batches: every rank's routes
-    E.rwts = take(sizeof(float) * (size_t)T * kTop);
-    E.rflags = take(sizeof(int) * kMaxRanks);                    // epoch whose routes each rank has sent
-    E.total = p;
+    E.flags = take(sizeof(int) * kMaxRanks);   // epoch reached by each source rank
+    E.epoch = take(sizeof(int) * 2);           // call epoch, combine ticket
+    E.rflags = take(sizeof(int) * kMaxRanks);  // epoch whose routes each rank has sent
+    E.rids = take(sizeof(int) * (size_t)kMaxTokens * kTop);  // large batches: every rank's routes
+    E.rwts = take(sizeof(float) * (size_t)kMaxTokens * kTop);
+    E.dslots = take(sizeof(float) * 2 * (size_t)kMaxDecodeTokens * kTop * H);  // [2][32*10][H]
+    E.dshout = take(sizeof(float) * 2 * (size_t)kMaxDecodeTokens * H);         // [2][32][H]
+    E.start = p;
+    return E;
+}
+
+// Large batches: this rank's slot rows [T*10][H] and shared rows [T][H] after
+// the per-call regions; returns the end of the workspace.
+struct EpLarge {
+    size_t slots, shout, total;
+};
+
+EpLarge ep_large(int T, int H, int F) {
+    EpLarge E{};
+    E.slots = align256(layout(T, H, F, ep_fixed(H).start).total);
+    E.shout = align256(E.slots + sizeof(float) * (size_t)T * kTop * H);
+    E.total = align256(E.shout + sizeof(float) * (size_t)T * H);
     return E;
 }
 
@@ -1367,9 +1399,12 @@ __device__ __forceinline__ int ld_acquire_sys(const int *p) {
 
 // grid (H/256, tokens from t0): out[t] = sum_k (rank order) slots[t][k] +
 // sigmoid(g_t) * shared[t] once every rank has raised its flag for this call.
+// cap > 0: the rows sit in the set of the epoch's parity (two sets of cap
+// tokens); cap = 0: one set. A wait that runs out sets error bit 8 and gives
+// the tokens NaN rows.
 __global__ void ep_combine_kernel(float *out, const float *slots, const float *shout, const int *ids,
                                   const int *expect, const float *sgate, int has_shared, int T, int H, int ranks,
-                                  const int *flags, int *epoch, int *err, int t0) {
+                                  const int *flags, int *epoch, int *err, int t0, int cap) {
     __shared__ int s_ok;
     const int t = t0 + blockIdx.y, d = blockIdx.x * blockDim.x + threadIdx.x;
     const int e = __ldcg(epoch);
@@ -1388,16 +1423,18 @@ __global__ void ep_combine_kernel(float *out, const float *slots, const float *s
         s_ok = ok;
     }
     __syncthreads();
-    if (s_ok && d < H) {
-        const size_t par = e & 1;
+    if (d < H && !s_ok) {
+        out[(size_t)t * H + d] = __int_as_float(0x7fc00000);
+    } else if (d < H) {
+        const size_t pt = (cap ? (size_t)(e & 1) * cap : 0) + t;
         const bool bad = (__ldcg(expect + t) & (1 << 16)) != 0;
         float sum = 0.0f;
 #pragma unroll
         for (int k = 0; k < kTop; k++) {
             const int id = __ldcg(ids + t * kTop + k);
-            sum += id >= 0 ? __ldcg(slots + ((par * T + t) * kTop + k) * H + d) : 0.0f;
+            sum += id >= 0 ? __ldcg(slots + (pt * kTop + k) * H + d) : 0.0f;
         }
-        if (has_shared) sum = __fmaf_rn(__ldcg(shout + (par * T + t) * H + d), sigmoidf_ref(__ldcg(sgate + t)), sum);
+        if (has_shared) sum = __fmaf_rn(__ldcg(shout + pt * H + d), sigmoidf_ref(__ldcg(sgate + t)), sum);
         out[(size_t)t * H + d] = bad ? __int_as_float(0x7fc00000) : sum;
     }
     // the epoch advances once every CTA has read it
@@ -1472,7 +1509,11 @@ __global__ void ep_routes_recv_kernel(int *ids, float *wts, const int *rids, con
 
 extern "C" int qg_ep_workspace_bytes(int tokens, int hidden, int ffn, size_t *bytes) {
     if (!bytes || check_shape(tokens, hidden, ffn)) return cudaErrorInvalidValue;
-    *bytes = ep_layout(tokens, hidden, ffn).total;
+    // every smaller batch fits too (each part grows with the token count)
+    const size_t start = ep_fixed(hidden).start;
+    size_t n = dec_layout(std::min(tokens, kMaxDecodeTokens), hidden, ffn, start).total;
+    if (tokens > kMaxDecodeTokens) n = std::max(n, ep_large(tokens, hidden, ffn).total);
+    *bytes = align256(n);
     return 0;
 }
 
@@ -1523,8 +1564,9 @@ extern "C" int qg_moe_layer_ep(float *out, int *ids_out, float *weights_out, con
         // its experts on the pairs routed to them and the shared expert on its own
         // tokens, stores each weighted row into the buffers of the token's rank,
         // and combines its own tokens once every rank has finished.
-        const Layout L = layout(tokens, hidden, ffn);
-        const EpLayout EL = ep_layout(tokens, hidden, ffn);
+        const EpFixed EF = ep_fixed(hidden);
+        const Layout L = layout(tokens, hidden, ffn, EF.start);
+        const EpLarge EL = ep_large(tokens, hidden, ffn);
         char *b = static_cast<char *>(workspace);
         float *logits = reinterpret_cast<float *>(b + L.logits);
         float *sgate = logits + (size_t)tokens * kExperts;
@@ -1540,7 +1582,7 @@ extern "C" int qg_moe_layer_ep(float *out, int *ids_out, float *weights_out, con
             if (!rc && sg) rc = launch_matmul(sgate + t0, s_router, 0, 1, hidden, xb, nb, st);
         }
         if (rc) return rc;
-        int *epoch = reinterpret_cast<int *>(b + EL.epoch);
+        int *epoch = reinterpret_cast<int *>(b + EF.epoch);
         {
             Span sp(kRoute, st);
             if (nb > 0 &&
@@ -1550,9 +1592,9 @@ extern "C" int qg_moe_layer_ep(float *out, int *ids_out, float *weights_out, con
             EpRoutes pr;
             for (int p = 0; p < ranks; p++) {
                 char *pb = static_cast<char *>(workspaces[p]);
-                pr.rids[p] = reinterpret_cast<int *>(pb + EL.rids);
-                pr.rwts[p] = reinterpret_cast<float *>(pb + EL.rwts);
-                pr.rflags[p] = reinterpret_cast<int *>(pb + EL.rflags);
+                pr.rids[p] = reinterpret_cast<int *>(pb + EF.rids);
+                pr.rwts[p] = reinterpret_cast<float *>(pb + EF.rwts);
+                pr.rflags[p] = reinterpret_cast<int *>(pb + EF.rflags);
             }
             ep_routes_send_kernel<<<ranks, 256, 0, st>>>(ids, wts, t0, t1, pr, rank, epoch);
             ep_routes_recv_kernel<<<16, 256, 0, st>>>(ids, wts, pr.rids[rank], pr.rwts[rank], tokens, ranks,
@@ -1562,12 +1604,12 @@ extern "C" int qg_moe_layer_ep(float *out, int *ids_out, float *weights_out, con
         }
         EpRun ep{};
         ep.local = expert_local, ep.n_local = n_local, ep.ranks = ranks, ep.rank = rank;
-        ep.block = block, ep.t0 = t0, ep.t1 = t1;
+        ep.block = block, ep.t0 = t0, ep.t1 = t1, ep.start = EF.start;
         for (int p = 0; p < ranks; p++) {
             char *pb = static_cast<char *>(workspaces[p]);
             ep.slots[p] = reinterpret_cast<float *>(pb + EL.slots);
             ep.shout[p] = reinterpret_cast<float *>(pb + EL.shout);
-            ep.flags[p] = reinterpret_cast<int *>(pb + EL.flags);
+            ep.flags[p] = reinterpret_cast<int *>(pb + EF.flags);
         }
         ep.epoch = epoch;
         if ((rc = run_experts(out, x, ids, wts, tokens, gate, gt, up, ut, down, dt, sg, sgt, su, sut, sd, sdt, sgate, 1,
@@ -1578,21 +1620,21 @@ extern "C" int qg_moe_layer_ep(float *out, int *ids_out, float *weights_out, con
             ep_combine_kernel<<<dim3((hidden + 255) / 256, ep.t1 - ep.t0), 256, 0, st>>>(
                 out, ep.slots[rank], ep.shout[rank], ids, reinterpret_cast<const int *>(b + L.expect), sgate,
                 sg != nullptr, tokens, hidden, ranks, ep.flags[rank], ep.epoch,
-                &reinterpret_cast<Header *>(b + L.hdr)->error, ep.t0);
+                &reinterpret_cast<Header *>(b + L.hdr)->error, ep.t0, 0);
         } else {  // no tokens here: still advance the call epoch after every rank's rows are in
             ep_combine_kernel<<<dim3(1, 1), 32, 0, st>>>(out, ep.slots[rank], ep.shout[rank], ids,
                                                          reinterpret_cast<const int *>(b + L.expect), sgate, 0, tokens,
                                                          0, ranks, ep.flags[rank], ep.epoch,
-                                                         &reinterpret_cast<Header *>(b + L.hdr)->error, 0);
+                                                         &reinterpret_cast<Header *>(b + L.hdr)->error, 0, 0);
         }
         return cudaGetLastError();
     }
-    const DecLayout DL = dec_layout(tokens, hidden, ffn);
-    const EpLayout EL = ep_layout(tokens, hidden, ffn);
+    const EpFixed EF = ep_fixed(hidden);
+    const DecLayout DL = dec_layout(tokens, hidden, ffn, EF.start);
     char *b = static_cast<char *>(workspace);
     int *ids = ids_out ? ids_out : reinterpret_cast<int *>(b + DL.ids);
     float *wts = weights_out ? weights_out : reinterpret_cast<float *>(b + DL.wts);
-    DecArgs a = dec_args(tokens, hidden, ffn, gt, dt, x, out, ids, wts, workspace);
+    DecArgs a = dec_args(tokens, hidden, ffn, gt, dt, x, out, ids, wts, workspace, EF.start);
     a.router = router;
     a.bias = logit_bias;
     a.s_router = sg ? s_router : nullptr;
@@ -1605,19 +1647,20 @@ extern "C" int qg_moe_layer_ep(float *out, int *ids_out, float *weights_out, con
     a.ep_local = expert_local;
     a.n_experts = n_local;
     a.ep_shared_here = rank == shared_rank;
-    a.ep_ranks = ranks, a.ep_rank = rank;
+    a.ep_ranks = ranks, a.ep_rank = rank, a.ep_cap = kMaxDecodeTokens;
     for (int p = 0; p < ranks; p++) {
         char *pb = static_cast<char *>(workspaces[p]);
-        a.ep_slots[p] = reinterpret_cast<float *>(pb + EL.slots);
-        a.ep_shout[p] = reinterpret_cast<float *>(pb + EL.shout);
-        a.ep_flags[p] = reinterpret_cast<int *>(pb + EL.flags);
+        a.ep_slots[p] = reinterpret_cast<float *>(pb + EF.dslots);
+        a.ep_shout[p] = reinterpret_cast<float *>(pb + EF.dshout);
+        a.ep_flags[p] = reinterpret_cast<int *>(pb + EF.flags);
     }
-    a.ep_epoch = reinterpret_cast<int *>(b + EL.epoch);
+    a.ep_epoch = reinterpret_cast<int *>(b + EF.epoch);
     int rc = dec_run_timed(a, st);
     if (rc) return rc;
+    Span sp(kCombine, st);  // includes the wait for the peers' rows
     ep_combine_kernel<<<dim3((hidden + 255) / 256, tokens), 256, 0, st>>>(
-        out, reinterpret_cast<const float *>(b + EL.slots), reinterpret_cast<const float *>(b + EL.shout), ids,
-        a.expect, a.sgate, sg != nullptr, tokens, hidden, ranks, reinterpret_cast<const int *>(b + EL.flags),
-        reinterpret_cast<int *>(b + EL.epoch), &a.hdr->error, 0);
+        out, reinterpret_cast<const float *>(b + EF.dslots), reinterpret_cast<const float *>(b + EF.dshout), ids,
+        a.expect, a.sgate, sg != nullptr, tokens, hidden, ranks, reinterpret_cast<const int *>(b + EF.flags),
+        reinterpret_cast<int *>(b + EF.epoch), &a.hdr->error, 0, kMaxDecodeTokens);
     return cudaGetLastError();
 }

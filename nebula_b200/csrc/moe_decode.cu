@@ -807,9 +807,9 @@ int sm_count() {
 
 namespace nb {
 
-DecLayout dec_layout(int T, int H, int F) {
+DecLayout dec_layout(int T, int H, int F, size_t start) {
     DecLayout L{};
-    size_t p = kPrefixBytes;
+    size_t p = start;
     auto take = [&](size_t bytes) {
         size_t at = p;
         p = (p + bytes + 255) & ~size_t(255);
@@ -900,7 +900,7 @@ int dec_run(const DecArgs &in, cudaStream_t st, cudaEvent_t split) {
         t.queue = &a.ctr->tc_queue, t.tc_ticket = &a.ctr->tc_ticket;
         t.gu_done = a.ctr->gu_done, t.tilecnt = a.ctr->tilecnt, t.err = &a.hdr->error;
         t.n_experts = a.n_experts;
-        t.ep_ranks = a.ep_ranks, t.ep_rank = a.ep_rank, t.ep_epoch = a.ep_epoch;
+        t.ep_ranks = a.ep_ranks, t.ep_rank = a.ep_rank, t.ep_cap = a.ep_cap, t.ep_epoch = a.ep_epoch;
         if (a.F / kTcRows <= kMaxGuTiles) t.gu_part = a.gu_part, t.gu_pcnt = a.ctr->gu_pcnt;
         for (int p = 0; p < kMaxRanks; p++)
             t.ep_slots[p] = a.ep_slots[p], t.ep_shout[p] = a.ep_shout[p], t.ep_flags[p] = a.ep_flags[p];

@@ -27,7 +27,9 @@ struct DecLayout {
     size_t logits, sgate, ids, wts, xpair, xsum, off, used, pairs, expect, mid, msum, slots, shout;
     size_t x16, xinv, xs16, sub, nsub, mid16, midinv, part, total;  // tensor-core path
 };
-DecLayout dec_layout(int T, int H, int F);
+// Regions from `start` (the fixed prefix by default; expert parallelism puts its
+// fixed cross-call block first and starts the per-call regions after it).
+DecLayout dec_layout(int T, int H, int F, size_t start = kPrefixBytes);
 
 struct DecArgs {
     int T, H, F, QG, QD;
@@ -54,6 +56,7 @@ struct DecArgs {
     int n_experts;       // experts in gate/up/down
     int ep_shared_here;  // this rank computes the shared expert
     int ep_ranks, ep_rank;
+    int ep_cap;  // tokens per parity buffer of the ranks' slot/shared rows
     float *ep_slots[kMaxRanks], *ep_shout[kMaxRanks];
     int *ep_flags[kMaxRanks];
     int *ep_epoch;

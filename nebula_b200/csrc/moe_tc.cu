@@ -1065,13 +1065,14 @@ __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a,
             } else {
                 const int row = it.mt * kTcRows + rr;
                 if (a.ep_ranks) {
-                    // every rank's buffers for this call's parity; the combine kernel reduces
-                    const int par = __ldcg(a.ep_epoch) & 1;
+                    // every rank's buffers (this call's parity set when double-buffered);
+                    // the combine kernel reduces
+                    const size_t pbase = a.ep_cap ? (size_t)(__ldcg(a.ep_epoch) & 1) * a.ep_cap : 0;
 #pragma unroll 4
                     for (int j = et >> 7; j < it.n; j += 2) {
                         const float y = sv[j * kTcRows + rr];
-                        const size_t o = it.expert < 0 ? ((size_t)par * T + tb.tok[j]) * H + row
-                                                       : ((size_t)par * T * kTop + tb.slot[j]) * H + row;
+                        const size_t o = it.expert < 0 ? (pbase + tb.tok[j]) * H + row
+                                                       : (pbase * kTop + tb.slot[j]) * H + row;
                         const float v = it.expert < 0 ? y : y * tb.w[j];
                         if (a.ep_block > 0) {  // the token's owner only
                             const int p = tb.tok[j] / a.ep_block;

@@ -52,10 +52,12 @@ struct TcArgs {
     int *err;
     int n_experts;         // experts held in gate/up/down
     // Expert parallelism (ep_ranks > 0): the down tiles write their weighted
-    // rows into every rank's buffers (peer memory, double-buffered by the
-    // parity of the call epoch) instead of combining, and the last CTA raises
-    // this rank's flag in every rank; a separate combine kernel reduces.
-    int ep_ranks, ep_rank;
+    // rows into every rank's buffers (peer memory) instead of combining, and
+    // the last CTA raises this rank's flag in every rank; a separate combine
+    // kernel reduces. ep_cap > 0: the buffers hold two sets of ep_cap tokens'
+    // rows and a call uses the set of its epoch's parity; ep_cap = 0: one set
+    // indexed by the call's own tokens.
+    int ep_ranks, ep_rank, ep_cap;
     // ep_block > 0 (large batches): token t belongs to rank t / ep_block, and a
     // down tile stores each row only into its owner's buffers.
     int ep_block;
@@ -69,8 +71,8 @@ struct TcArgs {
     // order and finishes the tile. Null: whole tiles only.
     float *gu_part;
     int *gu_pcnt;
-    float *ep_slots[kMaxRanks];   // per rank: [2][T*10][H]
-    float *ep_shout[kMaxRanks];   // per rank: [2][T][H]
+    float *ep_slots[kMaxRanks];   // per rank: [2][ep_cap*10][H], or [T*10][H] when ep_cap = 0
+    float *ep_shout[kMaxRanks];   // per rank: [2][ep_cap][H], or [T][H]
     int *ep_flags[kMaxRanks];     // per rank: [kMaxRanks] epoch reached by each source rank
     const int *ep_epoch;          // this rank's call epoch (advanced by the combine)
 };
