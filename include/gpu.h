@@ -128,13 +128,18 @@ int qg_moe_routed(float *out, const float *x, const int *ids, const float *weigh
 /* qg_moe_routed without a caller workspace (no counterpart in the reference):
  * for callers that cannot allocate device memory where they call, e.g. a
  * runtime whose device memory another allocator reserves in full up front.
- * The library keeps one static 8 MiB scratch per device (a T <= 17 batch at
- * hidden 2048 / ffn 512 fits); shapes whose qg_moe_workspace_bytes exceed it
- * return cudaErrorInvalidValue before anything is launched. Nothing is
+ * The library keeps one static 8 MiB scratch per device: batches of up to 28
+ * tokens at hidden 2048 / ffn 512 and up to 23 at 2560 / 640 fit (verify
+ * batches of up to 17 fit both); shapes whose qg_moe_workspace_bytes exceed
+ * it return cudaErrorInvalidValue before anything is launched. Nothing is
  * allocated. The first call on a device looks the scratch up and zeroes it
  * (and synchronises), so make it before any stream capture. Calls share the
  * scratch: calls that overlap on the device (other streams, other host
- * threads) race. */
+ * threads) race. There is no status readout: a call that finds the previous
+ * call's bounded-wait timeout recorded in the scratch clears its counters
+ * before running (the failed call's rows are not repaired); invalid routes
+ * give NaN rows. cudaDeviceReset after using this entry point is not
+ * supported. */
 int qg_moe_routed_static(float *out, const float *x, const int *ids, const float *weights, int tokens,
                          const void *gate, int gate_type, const void *up, int up_type,
                          const void *down, int down_type, int hidden, int ffn);
@@ -159,7 +164,11 @@ int qg_moe_layer(float *out, int *ids_out, float *weights_out, const float *x, i
 
 /* Expert parallelism across the GPUs of one box (no counterpart in the
  * reference, which runs on one GPU): one process per GPU, every rank calls
- * qg_moe_layer_ep for the same tokens and layer. Each rank holds n_local
+ * qg_moe_layer_ep for the same tokens and layer. A workspace sized by
+ * qg_ep_workspace_bytes for the largest batch serves every smaller batch, in
+ * any order (verify batches change size from step to step): the state kept
+ * between calls and the rows peers write sit at offsets independent of the
+ * call's token count. Each rank holds n_local
  * experts (gate/up/down as for qg_moe_layer, n_local of them) and
  * expert_local[512] (device) gives each expert's index there, or -1 when
  * another rank holds it; one rank (shared_rank) computes the shared expert.
@@ -173,8 +182,10 @@ int qg_moe_layer(float *out, int *ids_out, float *weights_out, const float *x, i
  * once, allocated with qg_alloc) as seen from this process: this rank's own
  * pointer and the others mapped with qg_ep_ipc_open from the 64-byte handles
  * each rank exports with qg_ep_ipc_handle. Calls go in the same order on
- * every rank; a rank that stops makes the others' combines time out (error
- * bit 8 in qg_moe_status) instead of hanging. Q4_K only.
+ * every rank; a rank that stops makes the others' combines time out after
+ * 2 s (error bit 8: qg_moe_status returns cudaErrorLaunchTimeout) with NaN
+ * output rows instead of hanging; every rank then zeroes its workspace
+ * before the next call. Q4_K only.
  * Large batches (tokens > 32): rank r owns tokens [r*B, (r+1)*B) with
  * B = ceil(tokens / ranks); each rank computes the router logits and top-10
  * of its own tokens and sends their ids and weights to every rank (ids_out
@@ -212,6 +223,41 @@ int qg_moe_status(const void *workspace, int *invalid_tokens, int *selected, int
  * two kernels run without programmatic overlap. */
 int qg_moe_profile(int enable);
 int qg_moe_profile_read(int phase, double *total_ms, int *launches);
+
+/* ---- loading an all-resident model (no counterpart in the reference
+ * header; the reference's loader is qwen/qwen.c:108-146,324-369) -------- */
+
+/* Reads a COB_QWEN_INDEX_V1 weight index (the format and checks of
+ * qwen/qwen.c:108-146) and maps its weight files read-only. Returns
+ * cudaErrorFileNotFound for a missing index or weights file (or one of the
+ * wrong size) and cudaErrorInvalidValue for a malformed index; `message`
+ * (optional) receives a description. Host only. */
+int qg_index_open(const char *path, void **index, char *message, size_t message_bytes);
+void qg_index_close(void *index);
+/* A tensor of the index by name (e.g. "blk.12.ffn_gate_exps.weight"): its
+ * bytes in the mapped file, GGML type, dims (dims[0] = row length) and size.
+ * cudaErrorInvalidValue when absent. */
+int qg_index_tensor(const void *index, const char *name, const void **host, int *type, uint64_t dims[4],
+                    uint64_t *bytes);
+/* Bulk upload of whole experts of one matrix: expert experts[i] (or i when
+ * experts is NULL), expert_bytes long at src + experts[i]*expert_bytes,
+ * lands at dst + i*expert_bytes. Loads all 512 experts of a layer, or one
+ * rank's experts under expert parallelism, through the uploader's pinned
+ * blocks (expert_bytes <= the size given to qg_upload_create) on the legacy
+ * default stream; returns once the last copy is queued. */
+int qg_upload_experts(void *uploader, void *dst, const void *src, size_t expert_bytes, const int *experts,
+                      int count);
+
+/* QROUTE1 route traces (written by the reference's route profiler,
+ * qwen/qwen.c:87-94,638-646): qg_route_trace_next reads the next record -
+ * layer, target position, tokens, ids [tokens][10], weights [tokens][10] -
+ * into caller buffers of `capacity` tokens; *tokens = 0 at the end of the
+ * file; cudaErrorInvalidValue for a truncated record or more tokens than the
+ * capacity (or 8192). Host only. */
+int qg_route_trace_open(const char *path, void **trace);
+int qg_route_trace_next(void *trace, int *layer, int *position, int *tokens, int *ids, float *weights,
+                        int capacity);
+void qg_route_trace_close(void *trace);
 
 /* Synthetic weights for tests and benchmarks: rows x cols values drawn
  * N(0, stddev) from a counter-based generator keyed by seed, quantised on the

@@ -45,6 +45,12 @@ SIGNATURES = {
     "moe_status": ([P, C.POINTER(I), C.POINTER(I), C.POINTER(I)], I),
     "moe_profile": ([I], I), "moe_profile_read": ([I, C.POINTER(D), C.POINTER(I)], I),
     "synth_weights": ([P, I, I, I, U64, F], I), "synth_normal": ([P, Z, U64, F], I),
+    "index_open": ([C.c_char_p, C.POINTER(P), C.c_char_p, Z], I), "index_close": ([P], None),
+    "index_tensor": ([P, C.c_char_p, C.POINTER(P), C.POINTER(I), C.POINTER(U64), C.POINTER(U64)], I),
+    "upload_experts": ([P, P, P, Z, P, I], I),
+    "route_trace_open": ([C.c_char_p, C.POINTER(P)], I),
+    "route_trace_next": ([P, C.POINTER(I), C.POINTER(I), C.POINTER(I), P, P, I], I),
+    "route_trace_close": ([P], None),
 }
 
 _LIB = None
