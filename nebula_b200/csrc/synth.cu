@@ -1,12 +1,19 @@
 // Synthetic weights and activations for tests and benchmarks (qg_synth_*).
 //
-// Values are N(0, stddev) from a counter-based generator (splitmix64 hash of
-// seed and element index, Box-Muller), so any slice can be regenerated
-// independently and identically. Quantisation is this library's own simple
-// round-to-nearest scheme for the GGML Q4_K and IQ4_NL layouts; the
-// reference used llama.cpp's searched quantiser, which is not available here.
-// Kernel parity never depends on it: the CPU checker reads back the exact
-// bytes the device produced.
+// Values are approximately N(0, stddev) from a counter-based generator: the
+// sum of eight 16-bit uniforms taken from two splitmix64 hashes of the seed
+// and the element index (Irwin-Hall with n = 8, support +-4.9 stddev),
+// centred and scaled. Any slice can be regenerated independently and
+// identically. Quantisation is this library's own simple round-to-nearest
+// scheme for the GGML Q4_K and IQ4_NL layouts; the reference used llama.cpp's
+// searched quantiser, which is not available here. Kernel parity never
+// depends on it: the checkers read back the exact bytes the device produced.
+//
+// Every floating-point step is a single correctly rounded operation (integer
+// sums, int->float conversion, one multiply, IEEE divide, fp16 round to
+// nearest even; products that feed an add are written with __fmul_rn so no
+// multiply-add is contracted), so a host restatement reproduces the bytes
+// bit for bit.
 #include "quant.cuh"
 
 using namespace nb;
@@ -19,15 +26,18 @@ __device__ __forceinline__ uint64_t mix64(uint64_t z) {
     return z ^ (z >> 31);
 }
 
-// Element i of the stream `seed`: Box-Muller on a hashed pair of uniforms.
+// 1 / standard deviation of 2*S - 8*65535 for S a sum of eight uniform
+// 16-bit integers: 1 / (65536 * sqrt(8/3)).
+constexpr float kIhInvStd = 9.3440618e-06f;
+
+// Element i of the stream `seed`.
 __device__ inline float normal_at(uint64_t seed, uint64_t i, float stddev) {
-    uint64_t h = mix64(seed * 0xd1342543de82ef95ULL ^ mix64(i >> 1));
-    float u1 = ((uint32_t)(h >> 40) + 1u) * (1.0f / 16777216.0f);  // (0, 1]
-    float u2 = (uint32_t)(h & 0xffffffu) * (1.0f / 16777216.0f);    // [0, 1)
-    float r = sqrtf(-2.0f * logf(u1));
-    float s, c;
-    sincospif(2.0f * u2, &s, &c);
-    return stddev * r * ((i & 1) ? s : c);
+    const uint64_t k = seed * 0xd1342543de82ef95ULL;
+    const uint64_t h1 = mix64(k ^ mix64(2 * i)), h2 = mix64(k ^ mix64(2 * i + 1));
+    int64_t s = 0;
+    for (int j = 0; j < 4; j++) s += (int64_t)((h1 >> (16 * j)) & 0xffff) + (int64_t)((h2 >> (16 * j)) & 0xffff);
+    const int c = (int)(2 * s - 8 * 65535);  // odd, |c| < 2^20: exact as a float
+    return __fmul_rn(__int2float_rn(c), __fmul_rn(stddev, kIhInvStd));
 }
 
 __global__ void normal_kernel(float *dst, size_t n, uint64_t seed, float stddev) {
@@ -77,7 +87,8 @@ __global__ void q4k_kernel(unsigned char *dst, int rows, int cols, uint64_t seed
         }
         for (int i = 0; i < 4; i++) {
             const int g0 = 2 * i, g1 = 2 * i + 1;
-            const float ds0 = d * sc[g0], dm0 = dmin * mc[g0], ds1 = d * sc[g1], dm1 = dmin * mc[g1];
+            const float ds0 = __fmul_rn(d, (float)sc[g0]), dm0 = __fmul_rn(dmin, (float)mc[g0]);
+            const float ds1 = __fmul_rn(d, (float)sc[g1]), dm1 = __fmul_rn(dmin, (float)mc[g1]);
             for (int l = 0; l < 32; l++) {
                 float v0 = normal_at(seed, first + g0 * 32 + l, stddev);
                 float v1 = normal_at(seed, first + g1 * 32 + l, stddev);
@@ -113,7 +124,7 @@ __global__ void iq4nl_kernel(unsigned char *dst, int rows, int cols, uint64_t se
             int best = 0;
             float err = INFINITY;
             for (int c = 0; c < 16; c++) {
-                float e = fabsf(d * (float)kIq4nl[c] - v);
+                float e = fabsf(__fmul_rn(d, (float)kIq4nl[c]) - v);
                 if (e < err) {
                     err = e;
                     best = c;

@@ -1,9 +1,12 @@
 """TEST INFRASTRUCTURE ONLY - builds the CPU checker for the routed-MoE path.
 
-Two products:
+Three products:
 
 * ``oracle/_build/librestate.so`` from ``oracle/restate.c`` (our C restatement
   of the reference's device-side routing steps). Builds anywhere with gcc.
+* ``oracle/_build/libsynth.so`` from ``oracle/synth.c``: the library's
+  synthetic weight generator restated on the host, bit for bit, so CPU
+  baselines run on the GPU arm's exact bytes without the product library.
 * ``oracle/_ref/libqwen_cpu_<H>x<F>.so``: the reference's own CPU MoE
   (``qwen/cpu.c`` + ``cpu_dispatch.c``), compiled from the reference tree the
   way its ``qwen/Makefile:24-41`` does (three ISA objects with private
@@ -66,6 +69,26 @@ def build_restate() -> Path:
     return out
 
 
+def synth_path() -> Path:
+    return BUILD / "libsynth.so"
+
+
+def build_synth() -> Path:
+    """oracle/synth.c (host restatement of the synthetic generator): no multiply-add
+    contraction, so every float step rounds as the device's does."""
+    BUILD.mkdir(exist_ok=True)
+    out = synth_path()
+    src = HERE / "synth.c"
+    if not out.exists() or out.stat().st_mtime < src.stat().st_mtime:
+        cmd = ["gcc", "-O2", "-std=c11", "-Wall", "-Wextra", "-fPIC", "-shared", "-fopenmp", "-ffp-contract=off",
+               str(src), "-o", str(out)]
+        gomp = _gomp_dir()
+        if gomp:
+            cmd.append(f"-L{gomp}")
+        _run(cmd + ["-lgomp", "-lm"])
+    return out
+
+
 def build_ref(reference_root: Path, force: bool = False) -> list[Path]:
     """Compile the reference CPU MoE at both shapes. Returns the built libraries."""
     qdir = Path(reference_root) / "qwen"
@@ -113,7 +136,9 @@ def build_ref(reference_root: Path, force: bool = False) -> list[Path]:
 
 def main(argv: list[str]) -> int:
     build_restate()
-    ref = os.environ.get("NEBULA_REFERENCE", "/root/reference")
+    build_synth()
+    # the reference tree: $NEBULA_REFERENCE, else a "reference" directory beside the repository
+    ref = os.environ.get("NEBULA_REFERENCE") or str(Path(__file__).resolve().parents[2] / "reference")
     if Path(ref, "qwen", "cpu.c").exists():
         for p in build_ref(Path(ref), force="--force" in argv):
             print(p)

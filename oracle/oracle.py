@@ -228,3 +228,39 @@ def moe_layer(ref: RefCPU, rs: Restate, x: np.ndarray, router: np.ndarray,
         sgate = ref.matmul(sr, 0, 1, H, x, threads)
         rs.shared_add(out, sh, sgate)
     return out, ids, w, logits
+
+
+class Synth:
+    """``oracle/synth.c``: the library's synthetic generator restated on the host,
+    bit for bit (``qg_synth_weights`` / ``qg_synth_normal``)."""
+
+    def __init__(self):
+        path = _build.build_synth() if not _build.synth_path().exists() else _build.synth_path()
+        self.lib = lib = C.CDLL(str(path))
+        lib.or_synth_normal.argtypes = [P, C.c_uint64, C.c_uint64, C.c_uint64, F]
+        lib.or_synth_normal.restype = None
+        lib.or_synth_weights.argtypes = [P, I, I, C.c_uint64, F, C.c_int64, C.c_int64]
+        lib.or_synth_weights.restype = I
+
+    @staticmethod
+    def row_bytes(typ: int, cols: int) -> int:
+        return {0: cols * 4, 12: cols // 256 * 144, 20: cols // 32 * 18}[typ]
+
+    def weights(self, typ: int, rows: int, cols: int, seed: int, stddev: float = 0.02,
+                out: np.ndarray | None = None, row0: int = 0, nrows: int | None = None) -> np.ndarray:
+        """Rows [row0, row0+nrows) of the rows x cols matrix into ``out`` (a flat uint8
+        array of the whole matrix; allocated when None, untouched outside those rows)."""
+        rb = self.row_bytes(typ, cols)
+        if out is None:
+            out = np.empty(rows * rb, np.uint8)
+        nrows = rows - row0 if nrows is None else nrows
+        if row0 < 0 or nrows < 0 or row0 + nrows > rows or out.nbytes < rows * rb:
+            raise ValueError("row range outside the matrix")
+        if self.lib.or_synth_weights(out.ctypes.data + row0 * rb, typ, cols, seed, stddev, row0, nrows):
+            raise ValueError("or_synth_weights")
+        return out
+
+    def normal(self, count: int, seed: int, stddev: float = 1.0) -> np.ndarray:
+        out = np.empty(count, np.float32)
+        self.lib.or_synth_normal(out.ctypes.data, 0, count, seed, stddev)
+        return out

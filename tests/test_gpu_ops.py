@@ -271,3 +271,23 @@ def test_upload_expert_packs_gate_up_down(L):
         assert L.code("upload_expert", up, dst.p, parts[0].ctypes.data, total + 1, None, 0, None, 0) != 0
     finally:
         L.load().qg_upload_destroy(up)
+
+
+@pytest.mark.parametrize("typ,rows,cols,seed,std", ((12, 640, 2048, 901, 0.02), (20, 300, 2048, 17, 0.02),
+                                                   (0, 512, 2048, 904, 0.02), (12, 2048, 512, 3, 0.02),
+                                                   (20, 2560, 640, 8, 0.5)))
+def test_host_synth_restatement_matches_device_bytes(L, typ, rows, cols, seed, std):
+    """oracle/synth.c gives the device generator's bytes bit for bit, so the CPU
+    baselines can run on the GPU arm's exact layers."""
+    from oracle.oracle import Synth
+    dev = L.synth_weights(typ, rows, cols, seed, std).get()
+    host = Synth().weights(typ, rows, cols, seed, std)
+    np.testing.assert_array_equal(dev, host)
+    # a row range alone, as the CPU baselines generate the experts they need
+    part = np.zeros_like(host)
+    Synth().weights(typ, rows, cols, seed, std, out=part, row0=rows // 3, nrows=rows // 4)
+    rb = host.nbytes // rows
+    lo, hi = rows // 3 * rb, (rows // 3 + rows // 4) * rb
+    np.testing.assert_array_equal(part[lo:hi], host[lo:hi])
+    x = L.synth_normal(100_003, seed + 1).get()
+    np.testing.assert_array_equal(x, Synth().normal(100_003, seed + 1))
