@@ -185,7 +185,6 @@ int launch_matmul(float *o, const void *w, int type, int rows, int cols, const f
         const float *wf = static_cast<const float *>(w);
         if (rows >= 32) return launch_tiled<32, 32>(o, wf, rows, cols, x, nt, st);
         return launch_tiled<8, 16>(o, wf, rows, cols, x, nt, st);
-        return cudaGetLastError();
     }
     dim3 grid((rows + kRowsPerCta - 1) / kRowsPerCta, (nt + kTokTile - 1) / kTokTile);
     const unsigned char *wb = static_cast<const unsigned char *>(w);

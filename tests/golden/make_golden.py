@@ -125,5 +125,7 @@ def main(reference_root: Path) -> None:
 
 
 if __name__ == "__main__":
-    root = Path(sys.argv[1] if len(sys.argv) > 1 else os.environ.get("NEBULA_REFERENCE", "/root/reference"))
+    # the reference tree: argv[1], $NEBULA_REFERENCE, else a "reference" directory beside the repository
+    root = Path(sys.argv[1] if len(sys.argv) > 1 else
+                os.environ.get("NEBULA_REFERENCE") or Path(__file__).resolve().parents[3] / "reference")
     main(root)
