@@ -14,7 +14,10 @@ namespace nb {
 
 // Launch stream of the calling host thread: 0 (legacy default stream) unless a
 // qg_graph_begin capture is active on this thread (reference qwen/gpu.cu:10).
-extern thread_local cudaStream_t launch_stream;
+// Its symbol is fixed (nebula_launch_stream) so that code linked into the same
+// library - the reference's non-MoE kernels in the qwen.c integration build -
+// can launch on the same per-thread stream and join the same captures.
+extern thread_local cudaStream_t launch_stream asm("nebula_launch_stream");
 
 constexpr int kExperts = 512;
 constexpr int kTop = 10;

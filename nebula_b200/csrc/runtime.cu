@@ -12,7 +12,7 @@
 #include "common.cuh"
 
 namespace nb {
-thread_local cudaStream_t launch_stream = 0;
+thread_local cudaStream_t launch_stream asm("nebula_launch_stream") = 0;
 }
 using nb::launch_stream;
 
