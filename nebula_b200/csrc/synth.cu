@@ -115,9 +115,6 @@ __global__ void iq4nl_kernel(unsigned char *dst, int rows, int cols, uint64_t se
         }
         unsigned short dh = f16_bits(ext / -127.0f);
         float d = __half2float(__ushort_as_half(dh));
-        unsigned char *p = dst + b * 18;
-        p[0] = dh & 255;
-        p[1] = dh >> 8;
         unsigned char q[32];
         for (int l = 0; l < 32; l++) {
             float v = normal_at(seed, first + l, stddev);
@@ -132,7 +129,16 @@ __global__ void iq4nl_kernel(unsigned char *dst, int rows, int cols, uint64_t se
             }
             q[l] = (unsigned char)best;
         }
-        for (int j = 0; j < 16; j++) p[2 + j] = (unsigned char)(q[j] | (q[j + 16] << 4));
+        // the 18-byte block as nine little-endian 16-bit words (blocks start on even
+        // addresses): d, then code bytes j = 0..15 holding values j (low nibble) and
+        // j+16 (high nibble)
+        unsigned short *p16 = reinterpret_cast<unsigned short *>(dst + b * 18);
+        p16[0] = dh;
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            const unsigned lo = q[2 * i] | (q[2 * i + 16] << 4), hi = q[2 * i + 1] | (q[2 * i + 17] << 4);
+            p16[1 + i] = (unsigned short)(lo | (hi << 8));
+        }
     }
 }
 }  // namespace
@@ -146,6 +152,7 @@ extern "C" int qg_synth_normal(float *dst, size_t count, uint64_t seed, float st
 
 extern "C" int qg_synth_weights(void *dst, int type, int rows, int cols, uint64_t seed, float stddev) {
     if (!dst || rows < 1 || !row_bytes(type, cols)) return cudaErrorInvalidValue;
+    if (type == 20 && (reinterpret_cast<uintptr_t>(dst) & 1)) return cudaErrorInvalidValue;  // 16-bit stores
     unsigned char *p = static_cast<unsigned char *>(dst);
     if (type == 0) {
         normal_kernel<<<1184, 256, 0, launch_stream>>>(reinterpret_cast<float *>(p), (size_t)rows * cols, seed, stddev);
