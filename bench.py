@@ -97,16 +97,18 @@ def measured_peaks() -> dict:
     return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
 
 
-def traffic_per_launch(kernel: str, workload: str) -> tuple[float | None, str | None]:
-    """DRAM bytes per launch from the committed ncu summary (profiles/traffic.txt:
-    lines 'kernel workload bytes_per_launch source...')."""
+def traffic_per_launch(kernel: str, workload: str, alg_bytes: float) -> tuple[float | None, str | None]:
+    """DRAM bytes per launch: the committed ncu ratio of traffic to algorithmic bytes
+    (profiles/traffic.txt: 'kernel workload ratio notes...') times this launch's
+    algorithmic bytes."""
     p = ROOT / "profiles" / "traffic.txt"
     if not p.exists():
         return None, None
     for line in p.read_text().splitlines():
         f = line.split()
-        if len(f) >= 4 and not line.startswith("#") and f[0] == kernel and f[1] == workload:
-            return float(f[2]), " ".join(f[3:])
+        if len(f) >= 3 and not line.startswith("#") and f[0] == kernel and f[1] == workload:
+            return float(f[2]) * alg_bytes, ("ncu dram__bytes_read.sum + dram__bytes_write.sum, 2-layer capture, "
+                                             f"{float(f[2]):.4f} x the algorithmic bytes (profiles/traffic.txt)")
     return None, None
 
 
@@ -611,7 +613,7 @@ def main() -> None:
     total_prof_ms = sum(v[0] for v in prof.values())
     stack_bytes = sum(layer_bytes(u, T) for u in used)
     traffic, traffic_src = traffic_per_launch("tc_experts_kernel<24>" if dom == "experts" else dom,
-                                              f"T{T}_ep{world}" if ep_mode else f"T{T}")
+                                              f"T{T}_ep{world}" if ep_mode else f"T{T}", dom_bytes)
     phase_us = {k: max_over_ranks(1e3 * v[0] / args.steps / args.layers) for k, v in sorted(prof.items()) if v[1]}
 
     # e2e through the C ABI with pinned host buffers
