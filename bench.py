@@ -533,6 +533,9 @@ def main() -> None:
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--no-configs", action="store_true", help="skip configs 1, 2, the T sweep and the product shape")
+    ap.add_argument("--routes", default=None,
+                    help="also replay this QROUTE1 route trace (the reference's route profiler output) through "
+                         "qg_moe_routed on the stack's layers (record layer modulo the stack depth)")
     ap.add_argument("--clock-log", default=None,
                     help="write the NVML clock samples of the timed region as CSV here ({rank} is replaced)")
     args = ap.parse_args()
@@ -803,6 +806,35 @@ def main() -> None:
         configs["sweep_T1_17"] = {"workload": "config 3: the 48-layer stack at T = 1..17 (graph per T)",
                                   "points": sweep}
 
+    trace_replay = None
+    if args.routes and world == 1:
+        from nebula_b200 import trace as tr
+        xcache = {}
+
+        def x_of(layer, nt):
+            if nt not in xcache:
+                xcache[nt] = L.synth_normal(nt * H, 9000 + nt)
+            return xcache[nt]
+
+        def experts_of(layer):
+            d = stack.w[layer % args.layers]
+            return d["gate"], Q4K, d["up"], Q4K, d["down"], Q4K
+
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        nrec = ntok = 0
+        torch.cuda.synchronize()
+        a.record()
+        for _layer, _pos, _out, _ws in tr.replay(args.routes, experts_of, x_of, H, F):
+            nrec += 1
+            ntok += _out.shape[0]
+        b.record()
+        torch.cuda.synchronize()
+        rms = a.elapsed_time(b)
+        trace_replay = {"file": os.path.basename(args.routes), "records": nrec, "token_layers": ntok,
+                        "ms": rms, "token_layers_per_s": ntok / (rms / 1e3),
+                        "note": "recorded routing through qg_moe_routed on the stack's resident experts; "
+                                "includes the host's per-record uploads of ids and weights"}
+
     line = {
         "metric": "moe_verify_tokens_per_s", "value": value, "unit": "tokens/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
@@ -834,6 +866,8 @@ def main() -> None:
         line["cpu_baseline"] = cpu
     if configs:
         line["configs"] = configs
+    if trace_replay:
+        line["trace_replay"] = trace_replay
     if rank == 0:
         print(json.dumps(line), flush=True)
     L.load().qg_graph_destroy(graph)
