@@ -521,6 +521,48 @@ def single_layer_config(torch, L, peaks, T: int, h: int, f: int, gt: int, dt: in
     return res
 
 
+def prefill_product(torch, L, peaks, cpu: bool, cpu_seconds: float, steps: int) -> dict:
+    """Prefill of the production mix (hidden 2560 / FFN 640, Q4_K gate/up + IQ4_NL down): one
+    layer at T=2048 routed from N(0,1) logits (about 40 tokens per expert), routed experts only,
+    with parity and the reference CPU MoE on the same bytes."""
+    P, h, f, seed0 = 2048, 2560, 640, 14
+    st = Stack(L, 1, P, seed0=seed0, h=h, f=f, gt=Q4K, dt=IQ4NL, shared=False, bias=False)
+    d0 = st.w[0]
+    logits = np.random.default_rng(5).normal(0, 1, (P, E)).astype(np.float32)
+    dl = L.Device(logits)
+
+    def pre():
+        L.call("route", d0["ids"].p, d0["wts"].p, dl.p, P)
+        L.call("moe_routed", d0["out"].p, d0["x"].p, d0["ids"].p, d0["wts"].p, P, d0["gate"].p, Q4K, d0["up"].p,
+               Q4K, d0["down"].p, IQ4NL, h, f, st.ws.p)
+
+    for _ in range(3):
+        pre()
+    pms = event_ms(torch, pre, max(3, steps // 4))
+    pbytes = E * expert_bytes(h, f, Q4K, IQ4NL) + 2 * P * h * 4 + P * K * 8
+    flops = P * K * 3 * h * f * 2
+    res = {"workload": "product-shape prefill: 1 layer, T=2048, hidden 2560 / FFN 640, Q4_K gate/up + IQ4_NL "
+                       "down, N(0,1) logits -> top-10, 512 experts",
+           "tokens_per_s": P / (pms / 1e3), "ms_per_layer": pms,
+           "hbm_gbs": pbytes / (pms / 1e3) / 1e9, "hbm_frac": pbytes / (pms / 1e3) / 1e9 / peaks["hbm_gbs"],
+           "tflops": flops / (pms / 1e3) / 1e12, "tensor_frac": flops / (pms / 1e3) / 1e12 / peaks["bf16_tflops"],
+           "path": "tcgen05 tensor-core expert kernel (IQ4_NL down as fp16 hi/lo planes of d*code)"}
+    if cpu:
+        cores = host_cores()
+        hl = HostLayers(P, seed0=seed0, h=h, f=f, gt=Q4K, dt=IQ4NL, shared=False, bias=False)
+        dp = hl.layer(0, P, all_experts=True, logits=logits)
+        out_c, ids_c = hl.run(dp, route=False)
+        res["parity"] = parity(d0["out"].get(), out_c, d0["ids"].get(), ids_c)
+        c = time_cpu_layers(hl, [dp], cpu_seconds, min_evals=2, route=False)
+        res["cpu_baseline"] = cpu_line(P / c["per_layer_s"], cores,
+                                       f"{c['evals']} evaluations of the same layer (same bytes, qc_moe large-batch "
+                                       f"path); backend {c['backend']}")
+        del dp
+    del st
+    L.call("sync")
+    return res
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -792,6 +834,7 @@ def main() -> None:
             torch, L, peaks, 17, 2560, 640, Q4K, IQ4NL, True, 13, want_cpu, 3.0,
             "product shape: 1 layer, T=17, hidden 2560 / FFN 640, Q4_K gate/up + IQ4_NL down, router + shared "
             "expert", args.steps)
+        configs["product_prefill"] = prefill_product(torch, L, peaks, want_cpu, 4.0, args.steps)
         sweep = {}
         for t in range(1, T + 1):
             g = stack.capture(t)

@@ -350,19 +350,6 @@ __device__ __forceinline__ void q4k_word(uint32_t w, float2 (&q)[4]) {
                       make_float2(-32768.0f, -2048.0f));
 }
 
-// IQ4_NL: four codes (one per byte of q, each < 16) -> code-book value + 128
-// per byte, selected with byte permutes from two 8-entry halves.
-__device__ __forceinline__ uint32_t iq4_lut4(uint32_t q) {
-    // code book + 128: 1,24,45,63,79,93,106,118 | 129,141,153,166,181,197,217,241
-    constexpr uint32_t T0 = 0x3F2D1801u, T1 = 0x766A5D4Fu, T2 = 0xA6998D81u, T3 = 0xF1D9C5B5u;
-    const uint32_t s = q & 0x07070707u;
-    const uint32_t n = s | (s >> 4);
-    const uint32_t sel = __byte_perm(n, 0, 0x0020);
-    const uint32_t lo = __byte_perm(T0, T1, sel), hi = __byte_perm(T2, T3, sel);
-    uint32_t mask;  // 0xFF where the code is >= 8: prmt replicates bit 7 of each byte (selector msb set)
-    asm("prmt.b32 %0, %1, 0, %2;" : "=r"(mask) : "r"(q << 4), "r"(0xBA98u));
-    return (hi & mask) | (lo & ~mask);
-}
 // byte b of (lo4, hi4) -> exact code-book values (low nibble, high nibble)
 __device__ __forceinline__ float2 iq4_pair(uint32_t lo4, uint32_t hi4, int b) {
     const uint32_t sel = 0x7650u | (uint32_t)b;  // byte b, then bytes 1..3 of 0x4B000000
@@ -888,7 +875,7 @@ int dec_run(const DecArgs &in, cudaStream_t st, cudaEvent_t split) {
         TcArgs t{};
         t.T = a.T, t.H = a.H, t.F = a.F;
         t.gate = a.gate, t.up = a.up, t.down = a.down, t.sg = a.sg, t.su = a.su, t.sd = a.sd;
-        t.grb = a.grb, t.drb = a.drb;
+        t.grb = a.grb, t.drb = a.drb, t.dn_iq4 = a.QD == 20;
         t.all_tok = 1;
         t.x16 = a.x16, t.xinv = a.xinv, t.xsum = a.xsum, t.xs16 = a.xs16;
         t.mi_stride = ((a.F / 128) + 3) & ~3;

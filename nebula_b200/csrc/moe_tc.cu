@@ -1,5 +1,7 @@
 // Tensor-core (tcgen05) expert kernel for Q4_K routed experts and the shared
-// expert, used by both the decode and the prefill paths.
+// expert, used by both the decode and the prefill paths. The down weights may
+// instead be IQ4_NL (the production mix: Q4_K gate/up, IQ4_NL down, ffn 640):
+// see the IQ4_NL notes below.
 //
 // Work items (claimed from a device queue, shared expert first): a gate/up
 // tile = 128 rows of W_gate and of W_up of one expert x one token tile of up
@@ -42,9 +44,16 @@
 //   warps 12-19     epilogue (warp w reads TMEM lanes 32*(w%4).., half the
 //                   tokens each); a tile's per-token outputs go through a
 //                   shared buffer so the per-token loops stay short
+// IQ4_NL down (DIQ): each 32-value block's fp16 scale d is folded into A as
+// two fp16 planes, hi = fp16(d*c) and lo = d*c - hi (exact), issued as two
+// MMAs into the same accumulator; the epilogue then applies only the B scale.
+// A down tile's 128 rows (ffn/32 blocks of 18 bytes each, not a multiple of
+// 16 bytes) arrive in one bulk copy, and an ffn of 640 ends in a half step of
+// 128 values.
 // Every wait is bounded; on a timeout the CTA raises the error word, stops
 // taking work, drains its copies and MMAs, frees TMEM and exits.
 #include <algorithm>
+#include <cstring>
 #include "moe_tc.cuh"
 #include "quant.cuh"
 
@@ -62,13 +71,20 @@ constexpr int kRegsLaunch = 96, kRegsLow = 64, kRegsEpi = 144;
 static_assert((kWarps - kEpiWarps) * kRegsLow + kEpiWarps * kRegsEpi == kWarps * kRegsLaunch, "register split");
 static_assert(kEpiWarp0 % 4 == 0 && kEpiWarps % 4 == 0, "register split is per warpgroup");
 constexpr int kSbBytes = kTcRows * 144;           // one superblock of 128 Q4_K rows
-constexpr int kRawStage = 2 * kSbBytes;           // gate + up
-constexpr int kRawStages = 3;
 constexpr int kOffRaw = 0;
 constexpr int kScRows = 2 * kTcRows * 16;         // d, dmin, m[8] per row per matrix
-// Layout of one instantiation for token tiles of up to TOK tokens.
-template <int TOK>
+// IQ4_NL down rows (ffn/32 blocks of 18 bytes) need not be a multiple of 16
+// bytes long, so a down tile's 128 rows arrive whole in one bulk copy: up to
+// ffn = 640 (46,080 bytes).
+constexpr int kDiqMaxFfn = 640;
+constexpr int kDiqRawStage = kTcRows * kDiqMaxFfn / 32 * 18;
+// Layout of one instantiation for token tiles of up to TOK tokens; DIQ: the
+// down weights are IQ4_NL (gate/up stay Q4_K).
+template <int TOK, bool DIQ = false>
 struct Cfg {
+    // raw weight ring: a gate + up superblock, or (DIQ) a whole down tile
+    static constexpr int kRawStage = DIQ ? kDiqRawStage : 2 * kSbBytes;
+    static constexpr int kRawStages = (DIQ && TOK > 32) ? 2 : 3;
     // Decode tiles of kTcTokSmall tokens run the gate/up Q4_K min term
     // dmin*sum_g m_g*sum(x over g) on the tensor cores: per superblock one more
     // K=16 MMA per matrix, A'' = dmin*m_g*2^8 split hi/lo (exact in 22 bits), B'' =
@@ -95,6 +111,8 @@ struct Cfg {
     static_assert(kAStages >= 2 && kACol0 + kAStages * 64 <= 512, "tensor memory budget");
     static_assert(kSmem % 16 == 0 && kScSlot % 16 == 0 && kOffB % 1024 == 0 && kBBytes % 1024 == 0 &&
                       kBSlot % 1024 == 0 && (TOK * 128) % 1024 == 0 && (16 * TOK) % 128 == 0, "alignment");
+    // 227 KB per CTA, less about 4 KB of static shared memory (barriers, tables)
+    static_assert(kSmem <= 232448 - 4096, "shared memory budget");
 };
 constexpr int kTokDecode = 32;  // decode: every token tile has at most kMaxDecodeTokens tokens
 static_assert(kTokDecode <= kTcTok, "tile sizes");
@@ -109,7 +127,7 @@ struct Item {
 
 struct Bars {
     uint64_t item_full[4], item_empty[4], tab_full[4];
-    uint64_t raw_full[kRawStages], raw_empty[kRawStages];
+    uint64_t raw_full[3], raw_empty[3];  // up to three raw stages
     uint64_t a_full[4], a_empty[4];
     uint64_t b_full[8], b_empty[8];
     uint64_t d_full[2], d_empty[2];
@@ -277,6 +295,37 @@ __device__ __forceinline__ void q4k_half_cols(const unsigned char *row, int c, i
     }
 }
 
+// IQ4_NL: one 32-value block (fp16 d, then 16 code bytes: low nibbles are
+// values 0..15, high nibbles 16..31) of one row as 16 tensor-memory columns
+// per plane, column i holding values 2i and 2i+1: hi = fp16(d*c) and
+// lo = fp16(d*c - hi) for the code-book integer c. d*c has at most 18
+// significant bits and is a multiple of 2^-24, so lo is exact and
+// hi + lo == d*c (for |d| < 512, where d*c stays finite in fp16).
+__device__ __forceinline__ void iq4_block_cols(const unsigned char *blk, uint32_t (&hi)[16], uint32_t (&lo)[16]) {
+    const unsigned short *p16 = reinterpret_cast<const unsigned short *>(blk);  // blocks start on even bytes
+    const __half2 d2 = __half2half2(__ushort_as_half(p16[0]));
+    const __half2 bias = __half2half2(__ushort_as_half((unsigned short)0x6480u));  // 1152 = 1024 + 128
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const uint32_t w = (uint32_t)p16[1 + 2 * i] | ((uint32_t)p16[2 + 2 * i] << 16);  // code bytes 4i..4i+3
+#pragma unroll
+        for (int h = 0; h < 2; h++) {  // low nibbles: values 4i..4i+3; high nibbles: 16+4i..16+4i+3
+            const uint32_t cb = iq4_lut4(h ? (w >> 4) & 0x0F0F0F0Fu : w & 0x0F0F0F0Fu);  // code + 128 per byte
+#pragma unroll
+            for (int k = 0; k < 2; k++) {
+                // two codes as the fp16 pair (1024 + code + 128), then exact code-book values
+                uint32_t v = __byte_perm(cb, 0x64646464u, k ? 0x4342u : 0x4140u);
+                const __half2 c2 = __hsub2(*reinterpret_cast<const __half2 *>(&v), bias);
+                const __half2 h2 = __hmul2_rn(c2, d2);
+                const __half2 l2 = __hfma2(c2, d2, __hneg2(h2));
+                const int col = 8 * h + 2 * i + k;
+                hi[col] = *reinterpret_cast<const uint32_t *>(&h2);
+                lo[col] = *reinterpret_cast<const uint32_t *>(&l2);
+            }
+        }
+    }
+}
+
 // d, dmin and the eight 6-bit mins of one 144-byte superblock row.
 __device__ __forceinline__ uint4 q4k_row_scales(const unsigned char *row) {
     const uint4 hd = *reinterpret_cast<const uint4 *>(row);
@@ -338,12 +387,13 @@ struct __align__(16) TokTab {
     int ex[TOK];    // expected contributions of the token (down; combine counting)
 };
 
-template <int TOK>
+template <int TOK, bool DIQ>
 __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a, const __grid_constant__ TcMaps maps) {
-    using C = Cfg<TOK>;
+    using C = Cfg<TOK, DIQ>;
     constexpr int kTok = TOK, kBBytes = C::kBBytes, kScXs = C::kScXs, kScSlot = C::kScSlot, kOffB = C::kOffB,
                   kOffSc = C::kOffSc, kOffV = C::kOffV, kDCols = C::kDCols, kACol0 = C::kACol0,
-                  kAStages = C::kAStages, kBStages = C::kBStages;
+                  kAStages = C::kAStages, kBStages = C::kBStages, kRawStage = C::kRawStage,
+                  kRawStages = C::kRawStages;
     extern __shared__ __align__(1024) unsigned char smem[];
     __shared__ Bars bars;
     __shared__ Item items[4];
@@ -357,7 +407,11 @@ __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a,
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int T = a.T, H = a.H, F = a.F;
     const int gu_mt = F / kTcRows, dn_mt = H / kTcRows;
-    const int nsbk = H / 256, dn_sb = F / 256;  // superblocks of a whole gate/up tile, of a down tile
+    // superblocks (K steps of 256 values) of a whole gate/up tile, of a down tile
+    // (IQ4_NL down: ffn may end in a half step of 128 values)
+    const int nsbk = H / 256, dn_sb = (F + 255) / 256;
+    // 64-value chunks of step sb of a down tile
+    auto dn_chunks = [&](int sb) { return DIQ ? min(4, (F - 256 * sb) / 64) : 4; };
     if (tid == 0) {
         for (int i = 0; i < 4; i++) {
             mbar_init(&bars.item_full[i], 1);
@@ -461,8 +515,9 @@ __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a,
                 items[slot] = it;
                 arrive(&bars.item_full[slot]);
                 if (it.kind == kEnd) break;
-                const int nsb = it.kind == kGU ? it.nk : dn_sb;
-                for (int sb = 0; sb < nsb; sb++, gsb++) {
+                // raw units: one per superblock, or (IQ4_NL down) the whole tile
+                const int nraw = it.kind == kGU ? it.nk : DIQ ? 1 : dn_sb;
+                for (int sb = 0; sb < nraw; sb++, gsb++) {
                     const int st = gsb % kRawStages;
                     if (gsb >= kRawStages &&
                         !wait_phase(&bars.raw_empty[st], (gsb / kRawStages - 1) & 1, &abort_flag, err))
@@ -474,6 +529,11 @@ __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a,
                         const int x = (it.k0 + sb) * 144;
                         tma_2d(dst, it.expert < 0 ? &maps.sg : &maps.gate, x, y, &bars.raw_full[st]);
                         tma_2d(dst + kSbBytes, it.expert < 0 ? &maps.su : &maps.up, x, y, &bars.raw_full[st]);
+                    } else if (DIQ) {  // 128 whole rows: 128 * drb <= kRawStage bytes, 16-byte aligned
+                        const size_t row = (size_t)(it.expert < 0 ? 0 : it.expert * H) + it.mt * kTcRows;
+                        const uint32_t bytes = (uint32_t)(kTcRows * a.drb);
+                        mbar_arrive_expect_tx(&bars.raw_full[st], bytes);
+                        tma_load_1d(dst, (it.expert < 0 ? a.sd : a.down) + row * a.drb, bytes, &bars.raw_full[st]);
                     } else {
                         const int y = (it.expert < 0 ? 0 : it.expert * H) + it.mt * kTcRows;
                         mbar_arrive_expect_tx(&bars.raw_full[st], kSbBytes);
@@ -509,7 +569,8 @@ __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a,
                     if (gsb >= 2 && !(ok = wait_phase(&bars.d_empty[db], ((gsb >> 1) - 1) & 1, &abort_flag, err))) break;
                     tc_fence_after();
                     const uint32_t d = tmem + (uint32_t)((db * 2 + mi) * kDCols);
-                    for (int c = 0; c < 4; c++, gch++) {
+                    const int nch = gu ? 4 : dn_chunks(sb);
+                    for (int c = 0; c < nch; c++, gch++) {
                         const int ab = gch % kAStages, bs = gch % kBStages;
                         if (!(ok = wait_phase(&bars.a_full[ab], (gch / kAStages) & 1, &abort_flag, err))) break;
                         if (!(ok = wait_phase(&bars.b_full[bs], (gch / kBStages) & 1, &abort_flag, err))) break;
@@ -521,6 +582,12 @@ __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a,
                             mma_ts1(d, ac + 8, bd + 2, idesc);
                             mma_ts1(d, ac + 16, bd + 4, idesc);
                             mma_ts1(d, ac + 24, bd + 6, idesc);
+                            if (DIQ && !gu) {  // IQ4_NL down: the lo plane of A into the same D
+                                mma_ts1(d, ac + 32, bd, idesc);
+                                mma_ts1(d, ac + 40, bd + 2, idesc);
+                                mma_ts1(d, ac + 48, bd + 4, idesc);
+                                mma_ts1(d, ac + 56, bd + 6, idesc);
+                            }
                             if constexpr (C::kMinD2) {
                                 if (gu && c == 3) {  // min term into D2 (the item's first superblock starts it)
                                     if (sb == 0 && gu_items > 0 &&
@@ -602,7 +669,8 @@ __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a,
                     const int gsbk = gu ? it.k0 + sb : sb;  // superblock index along K
                     tma_2d(scb + kScRows, gs, gsbk * 8, brow, &bars.sc_full[sc_slot]);
                     tma_2d(scb + kScRows + kScXs, iv, gu ? 0 : (2 * sb) & ~3, brow, &bars.sc_full[sc_slot]);
-                    for (int c = 0; c < 4; c++, gch++) {
+                    const int nch = gu ? 4 : dn_chunks(sb);
+                    for (int c = 0; c < nch; c++, gch++) {
                         const int bs = gch % kBStages;
                         if (gch >= kBStages &&
                             !(ok = wait_phase(&bars.b_empty[bs], (gch / kBStages - 1) & 1, &abort_flag, err)))
@@ -634,7 +702,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a,
         const int ct = 32 * (warp & 3) + lane;           // weight row of the tile = TMEM lane
         const int nib = (warp - kConvWarp0) >> 2;        // 0: low nibbles + row scales, 1: high nibbles
         const uint32_t a_lanes = tmem + ((uint32_t)(32 * (warp & 3)) << 16) + kACol0 + nib * 16;
-        int gsb = 0, gch = 0;
+        int gsb = 0, gch = 0, graw = 0;  // superblocks, chunks, raw units
         for (int seq = 0;; seq++) {
             const int slot = seq & 3;
             if (!wait_phase(&bars.item_full[slot], (seq >> 2) & 1, &abort_flag, err)) break;
@@ -642,15 +710,22 @@ __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a,
             if (it.kind == kEnd) break;
             const int mats = it.kind == kGU ? 2 : 1;
             const int nsb = it.kind == kGU ? it.nk : dn_sb;
+            // IQ4_NL down: one raw unit holds the whole tile; this thread's row
+            const bool diq = DIQ && it.kind == kDN;
             bool ok = true;
+            int st = graw % kRawStages;
+            if (diq) ok = wait_phase(&bars.raw_full[st], (graw / kRawStages) & 1, &abort_flag, err);
             for (int sb = 0; sb < nsb && ok; sb++, gsb++) {
-                const int st = gsb % kRawStages, sc_slot = gsb & 3;
-                if (!(ok = wait_phase(&bars.raw_full[st], (gsb / kRawStages) & 1, &abort_flag, err))) break;
+                const int sc_slot = gsb & 3;
+                if (!diq) {
+                    st = graw % kRawStages;
+                    if (!(ok = wait_phase(&bars.raw_full[st], (graw / kRawStages) & 1, &abort_flag, err))) break;
+                }
                 const unsigned char *raw = smem + kOffRaw + st * kRawStage;
                 // row scales: matrix nib (gate by the low-nibble warps, up by the high-nibble ones)
                 if (gsb >= 4 && !(ok = wait_phase(&bars.sc_empty[sc_slot], ((gsb >> 2) - 1) & 1, &abort_flag, err)))
                     break;
-                if (nib < mats) {
+                if (nib < mats && !diq) {
                     uint4 *scs = reinterpret_cast<uint4 *>(smem + kOffSc + sc_slot * kScSlot);
                     scs[nib * kTcRows + ct] = q4k_row_scales(raw + nib * kSbBytes + ct * 144);
                 }
@@ -658,7 +733,8 @@ __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a,
                 if (lane == 0) arrive(&bars.sc_full[sc_slot]);
                 // kGrp chunks per store-completion wait (half the A ring)
                 constexpr int kGrp = kAStages >= 4 ? 2 : 1;
-                for (int c = 0; c < 4 && ok; c += kGrp, gch += kGrp) {
+                const int nch = diq ? dn_chunks(sb) : 4;
+                for (int c = 0; c < nch && ok; c += kGrp, gch += kGrp) {
                     for (int h = 0; h < kGrp; h++) {
                         const int g = gch + h, ab = g % kAStages;
                         if (g >= kAStages &&
@@ -670,10 +746,17 @@ __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a,
 #pragma unroll
                     for (int h = 0; h < kGrp; h++) {
                         const int ab = (gch + h) % kAStages;
-                        for (int m = 0; m < mats; m++) {
-                            uint32_t r[16];
-                            q4k_half_cols(raw + m * kSbBytes + ct * 144, c + h, nib, r);
-                            tmem_st16(a_lanes + (uint32_t)((ab * 2 + m) * 32), r);
+                        if (DIQ && diq) {  // block 2*chunk + nib of the row: hi plane, lo plane
+                            uint32_t rh[16], rl[16];
+                            iq4_block_cols(raw + ct * a.drb + (size_t)(2 * (4 * sb + c + h) + nib) * 18, rh, rl);
+                            tmem_st16(a_lanes + (uint32_t)((ab * 2) * 32), rh);
+                            tmem_st16(a_lanes + (uint32_t)((ab * 2 + 1) * 32), rl);
+                        } else {
+                            for (int m = 0; m < mats; m++) {
+                                uint32_t r[16];
+                                q4k_half_cols(raw + m * kSbBytes + ct * 144, c + h, nib, r);
+                                tmem_st16(a_lanes + (uint32_t)((ab * 2 + m) * 32), r);
+                            }
                         }
                     }
                     if constexpr (C::kMinD2) {
@@ -691,8 +774,16 @@ __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a,
                     if (lane == 0)
                         for (int h = 0; h < kGrp; h++) arrive(&bars.a_full[(gch + h) % kAStages]);
                 }
+                if (!diq) {
+                    __syncwarp();
+                    if (lane == 0) arrive(&bars.raw_empty[st]);
+                    graw++;
+                }
+            }
+            if (diq) {
                 __syncwarp();
                 if (lane == 0) arrive(&bars.raw_empty[st]);
+                graw++;
             }
             __syncwarp();
             if (lane == 0) arrive(&bars.item_empty[slot]);
@@ -865,6 +956,33 @@ __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a,
                                 float2 &ac = acc[m][cb * 4 + pp];
                                 ac = __ffma2_rn(d2, dot, ac);
                                 ac = __ffma2_rn(nm2, mt, ac);
+                            }
+                        }
+                    }
+                } else if (DIQ) {
+                    // IQ4_NL down: the block scales are in A; D[db][h] holds 128-value half h
+                    // of this step (a step at the end of ffn may have one half), each with
+                    // its own B scale
+                    const uint32_t c0 = lanes + (uint32_t)((db * 2) * kDCols);
+                    const int ioff = (2 * sb) & 3, nh = min(2, (F - 256 * sb) / 128);
+#pragma unroll
+                    for (int cb = 0; cb < kHalf / 8; cb++) {
+                        if (cb * 8 >= hw) break;
+#pragma unroll
+                        for (int h = 0; h < 2; h++) {
+                            if (h >= nh) break;
+                            uint32_t rh[8], rl[8];
+                            tmem_ld8_nw(c0 + h * kDCols + j0 + cb * 8, rh);
+                            tmem_ld8_nw(c0 + h * kDCols + kTok + j0 + cb * 8, rl);
+                            tmem_wait_ld();
+#pragma unroll
+                            for (int pp = 0; pp < 4; pp++) {
+                                if (cb * 8 + 2 * pp >= hw) break;
+                                const int j = j0 + cb * 8 + 2 * pp;
+                                const float2 v = __ffma2_rn(make_float2(__uint_as_float(rl[2 * pp]), __uint_as_float(rl[2 * pp + 1])), k2048,
+                                                            make_float2(__uint_as_float(rh[2 * pp]), __uint_as_float(rh[2 * pp + 1])));
+                                float2 &ac = acc[0][cb * 4 + pp];
+                                ac = __ffma2_rn(v, make_float2(inv4[j * 4 + ioff + h], inv4[j * 4 + 4 + ioff + h]), ac);
                             }
                         }
                     }
@@ -1234,10 +1352,10 @@ int sm_count_tc() {
 namespace nb {
 
 bool tc_supported(int H, int F, int QG, int QD) {
-    return QG == 12 && QD == 12 && H % 256 == 0 && F % 256 == 0 && H >= 256 && F >= 256 && encoder() != nullptr;
+    if (QG != 12 || H % 256 || H < 256 || F % kTcRows || F < kTcRows || encoder() == nullptr) return false;
+    if (QD == 12) return F % 256 == 0;
+    return QD == 20 && F <= kDiqMaxFfn;
 }
-
-size_t tc_smem_bytes() { return Cfg<kTcTok>::kSmem; }
 
 int tc_make_maps(const TcArgs &a, TcMaps &m, int tok) {
     const size_t E = a.n_experts > 0 ? a.n_experts : kExperts, H = a.H, F = a.F;
@@ -1245,12 +1363,20 @@ int tc_make_maps(const TcArgs &a, TcMaps &m, int tok) {
     const size_t xrows = a.all_tok ? (size_t)a.T : rows;  // rows of the gate/up activations
     const auto f16 = CU_TENSOR_MAP_DATA_TYPE_FLOAT16, f32 = CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
     const auto sw = CU_TENSOR_MAP_SWIZZLE_128B, none = CU_TENSOR_MAP_SWIZZLE_NONE;
+    // IQ4_NL down tiles arrive by plain bulk copies (rows need not be 16-byte multiples)
+    if (a.dn_iq4) {
+        if (a.F % kTcRows || a.F > kDiqMaxFfn || a.drb != (size_t)a.F / 32 * 18 ||
+            (reinterpret_cast<uintptr_t>(a.down) & 15) || (a.sd && (reinterpret_cast<uintptr_t>(a.sd) & 15)))
+            return cudaErrorInvalidValue;
+        memset(&m.down, 0, sizeof(m.down));
+        memset(&m.sd, 0, sizeof(m.sd));
+    }
     int rc = make_map(&m.gate, a.gate, E * a.F, a.grb);
     if (!rc) rc = make_map(&m.up, a.up, E * a.F, a.grb);
-    if (!rc) rc = make_map(&m.down, a.down, E * a.H, a.drb);
+    if (!rc && !a.dn_iq4) rc = make_map(&m.down, a.down, E * a.H, a.drb);
     if (!rc && a.sg) rc = make_map(&m.sg, a.sg, a.F, a.grb);
     if (!rc && a.sg) rc = make_map(&m.su, a.su, a.F, a.grb);
-    if (!rc && a.sg) rc = make_map(&m.sd, a.sd, a.H, a.drb);
+    if (!rc && a.sg && !a.dn_iq4) rc = make_map(&m.sd, a.sd, a.H, a.drb);
     if (!rc && !a.sg) {
         m.sg = m.gate;
         m.su = m.up;
@@ -1272,10 +1398,10 @@ int tc_make_maps(const TcArgs &a, TcMaps &m, int tok) {
     return rc;
 }
 
-template <int TOK>
+template <int TOK, bool DIQ>
 int tc_launch_tok(const TcArgs &a, const TcMaps &m, cudaStream_t st, bool pdl) {
-    constexpr int smem = Cfg<TOK>::kSmem;
-    int rc = cudaFuncSetAttribute(tc_experts_kernel<TOK>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    constexpr int smem = Cfg<TOK, DIQ>::kSmem;
+    int rc = cudaFuncSetAttribute(tc_experts_kernel<TOK, DIQ>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (rc) return rc;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(sm_count_tc());
@@ -1287,14 +1413,19 @@ int tc_launch_tok(const TcArgs &a, const TcMaps &m, cudaStream_t st, bool pdl) {
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, tc_experts_kernel<TOK>, a, m);
+    return cudaLaunchKernelEx(&cfg, tc_experts_kernel<TOK, DIQ>, a, m);
+}
+
+template <bool DIQ>
+int tc_launch_fmt(const TcArgs &a, const TcMaps &m, cudaStream_t st, bool pdl, int max_tile) {
+    if (max_tile <= kTcTokSmall) return tc_launch_tok<kTcTokSmall, DIQ>(a, m, st, pdl);
+    if (max_tile <= kTokDecode) return tc_launch_tok<kTokDecode, DIQ>(a, m, st, pdl);
+    if (max_tile <= kTcTok) return tc_launch_tok<kTcTok, DIQ>(a, m, st, pdl);
+    return cudaErrorInvalidValue;
 }
 
 int tc_launch(const TcArgs &a, const TcMaps &m, cudaStream_t st, bool pdl, int max_tile) {
-    if (max_tile <= kTcTokSmall) return tc_launch_tok<kTcTokSmall>(a, m, st, pdl);
-    if (max_tile <= kTokDecode) return tc_launch_tok<kTokDecode>(a, m, st, pdl);
-    if (max_tile <= kTcTok) return tc_launch_tok<kTcTok>(a, m, st, pdl);
-    return cudaErrorInvalidValue;
+    return a.dn_iq4 ? tc_launch_fmt<true>(a, m, st, pdl, max_tile) : tc_launch_fmt<false>(a, m, st, pdl, max_tile);
 }
 
 int tc_prep_launch(const float *x, int T, int H, __half *x16, float *xinv, float *xsum, cudaStream_t st) {

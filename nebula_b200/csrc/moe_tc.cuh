@@ -1,4 +1,4 @@
-// Tensor-core (tcgen05) expert kernel for Q4_K experts: interface.
+// Tensor-core (tcgen05) expert kernel for Q4_K experts (IQ4_NL down allowed): interface.
 #pragma once
 #include <cuda.h>
 #include "common.cuh"
@@ -19,8 +19,11 @@ struct SubJob {
 
 struct TcArgs {
     int T, H, F;
-    const unsigned char *gate, *up, *down, *sg, *su, *sd;  // Q4_K experts (+ shared), gate/up rows hold H values
+    // Q4_K gate/up rows of H values; down rows of F values, Q4_K or (dn_iq4)
+    // IQ4_NL; the shared expert (sg/su/sd) in the same formats
+    const unsigned char *gate, *up, *down, *sg, *su, *sd;
     size_t grb, drb;
+    int dn_iq4;
     // Gate/up activations: either per token (all_tok = 1: every gate/up tile
     // multiplies all T <= tile tokens and keeps its own columns) or per routed
     // row (rows as for the SwiGLU outputs below, filled by tc_prep_rows_launch).
@@ -78,14 +81,15 @@ struct TcArgs {
 };
 
 struct TcMaps {
-    CUtensorMap gate, up, down, sg, su, sd;  // raw Q4_K rows, one superblock x 128 rows per box
+    CUtensorMap gate, up, down, sg, su, sd;  // raw Q4_K rows, one superblock x 128 rows per box (down/sd unused for IQ4_NL)
     CUtensorMap bx_hi, bx_lo, bm_hi, bm_lo;  // B rows (activations, SwiGLU outputs), 64 values x tile rows, 128B swizzle
     CUtensorMap sx, sm, ix, im;              // their group sums (8 x tile rows) and scales (4 x tile rows)
     CUtensorMap gx_hi, gx_lo;                // xs16 hi and lo planes (8 x tile rows, no swizzle)
 };
 
+// Q4_K gate/up (hidden a multiple of 256, ffn of 128) with Q4_K down (ffn a
+// multiple of 256) or IQ4_NL down (ffn up to 640).
 bool tc_supported(int H, int F, int QG, int QD);
-size_t tc_smem_bytes();
 int tc_make_maps(const TcArgs &a, TcMaps &m, int max_tile);
 // max_tile: the largest token tile of the launch (sub-jobs, and the split of
 // the shared expert's tokens: shared sub-job i covers tokens i*max_tile ..).

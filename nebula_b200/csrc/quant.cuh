@@ -15,6 +15,19 @@ namespace nb {
 static __constant__ const signed char kIq4nl[16] = {-127, -104, -83, -65, -49, -35, -22, -10,
                                              1,    13,   25,  38,  53,  69,  89,  113};
 
+// IQ4_NL: four codes (one per byte of q, each < 16) -> code-book value + 128
+// per byte, selected with byte permutes from two 8-entry halves.
+__device__ __forceinline__ uint32_t iq4_lut4(uint32_t q) {
+    // code book + 128: 1,24,45,63,79,93,106,118 | 129,141,153,166,181,197,217,241
+    constexpr uint32_t T0 = 0x3F2D1801u, T1 = 0x766A5D4Fu, T2 = 0xA6998D81u, T3 = 0xF1D9C5B5u;
+    const uint32_t s = q & 0x07070707u;
+    const uint32_t n = s | (s >> 4);
+    const uint32_t sel = __byte_perm(n, 0, 0x0020);
+    const uint32_t lo = __byte_perm(T0, T1, sel), hi = __byte_perm(T2, T3, sel);
+    uint32_t mask;  // 0xFF where the code is >= 8: prmt replicates bit 7 of each byte (selector msb set)
+    asm("prmt.b32 %0, %1, 0, %2;" : "=r"(mask) : "r"(q << 4), "r"(0xBA98u));
+    return (hi & mask) | (lo & ~mask);
+}
 // Q4_K / Q5_K 6-bit scale and min of sub-block g from the 12 packed bytes.
 __device__ __forceinline__ void k_scale_min(const unsigned char *sc, int g, int &s, int &m) {
     if (g < 4) {

@@ -228,6 +228,33 @@ def test_layer_with_shared_expert(L, ref2048, restate, q4k_2048, T):
     assert_parity(out, e_out, f"layer T={T}")
 
 
+@pytest.mark.parametrize("T", (1, 17, 300))
+def test_layer_product_shape_with_shared_expert(L, ref2560, restate, prod_2560, T):
+    """The production mix at 2560/640 (Q4_K gate/up, IQ4_NL down, IQ4_NL shared
+    down) through the whole layer: decode (T <= 32) and the large-batch path."""
+    rng = np.random.default_rng(400 + T)
+    x = rng.normal(0, 1, (T, 2560)).astype(np.float32)
+    out, ids, w, ws = prod_2560.layer(x)
+    e_out, e_ids, e_w, _ = orc.moe_layer(ref2560, restate, x, prod_2560.hrouter, prod_2560.hgate, 12,
+                                         prod_2560.hup, 12, prod_2560.hdown, 20, shared=prod_2560.shared)
+    np.testing.assert_array_equal(ids, e_ids)
+    assert_parity(out, e_out, f"product layer T={T}")
+    inv, sel, used = L.status(ws)
+    assert inv == 0 and sel == T * 10 and used == len(np.unique(e_ids))
+
+
+def test_prefill_product_shape(L, ref2560, restate, prod_2560):
+    """Prefill of the production mix: T=2048, N(0,1) logits to top-10."""
+    rng = np.random.default_rng(5)
+    T = 2048
+    logits = rng.normal(0, 1, (T, 512)).astype(np.float32)
+    x = rng.normal(0, 1, (T, 2560)).astype(np.float32)
+    e_ids, e_w = restate.route(logits)
+    out, ws = prod_2560.routed(x, e_ids, e_w)
+    assert_parity(out, oracle_routed(ref2560, prod_2560, x, e_ids, e_w), "product prefill T=2048")
+    assert L.status(ws) == (0, T * 10, 512)
+
+
 def test_layer_zipf_bias(L, ref2048, restate, q4k_2048):
     """Config 3 routing skew: logits + bias, bias[perm[r]] = -1.1*ln(r+1)."""
     rng = np.random.default_rng(3)
