@@ -1075,7 +1075,7 @@ int run_experts(float *out, const float *x, const int *ids, const float *wts, in
         t.down = static_cast<const unsigned char *>(down);
         t.sg = static_cast<const unsigned char *>(sg), t.su = static_cast<const unsigned char *>(su);
         t.sd = static_cast<const unsigned char *>(sd);
-        t.grb = grb, t.drb = drb, t.dn_iq4 = dt == 20;
+        t.grb = grb, t.drb = drb, t.gu_iq4 = gt == 20, t.dn_iq4 = dt == 20;
         t.all_tok = T <= kTcTok;
         t.x16 = reinterpret_cast<__half *>(base + L.x16);
         t.xinv = reinterpret_cast<float *>(base + L.xinv);

@@ -846,7 +846,7 @@ bool dec_supported(int T, int H, int F, int QG, int QD) {
 
 int dec_run(const DecArgs &in, cudaStream_t st, cudaEvent_t split) {
     DecArgs a = in;
-    a.use_tc = tc_supported(a.H, a.F, a.QG, a.QD) && a.H / kTcRows <= 64;
+    a.use_tc = tc_supported(a.H, a.F, a.QG, a.QD, kMaxDecodeTokens) && a.H / kTcRows <= 64;
     const size_t grb = a.grb, drb = a.drb;
     a.gstride = (int)((grb + 127) / 128 * 128 + 16);  // rows start 16 bytes apart modulo 128
     const int gu_bytes = 2 * kGuRows * a.gstride;
@@ -875,7 +875,7 @@ int dec_run(const DecArgs &in, cudaStream_t st, cudaEvent_t split) {
         TcArgs t{};
         t.T = a.T, t.H = a.H, t.F = a.F;
         t.gate = a.gate, t.up = a.up, t.down = a.down, t.sg = a.sg, t.su = a.su, t.sd = a.sd;
-        t.grb = a.grb, t.drb = a.drb, t.dn_iq4 = a.QD == 20;
+        t.grb = a.grb, t.drb = a.drb, t.gu_iq4 = a.QG == 20, t.dn_iq4 = a.QD == 20;
         t.all_tok = 1;
         t.x16 = a.x16, t.xinv = a.xinv, t.xsum = a.xsum, t.xs16 = a.xs16;
         t.mi_stride = ((a.F / 128) + 3) & ~3;

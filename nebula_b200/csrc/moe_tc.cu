@@ -79,9 +79,10 @@ constexpr int kScRows = 2 * kTcRows * 16;         // d, dmin, m[8] per row per m
 constexpr int kDiqMaxFfn = 640;
 constexpr int kDiqRawStage = kTcRows * kDiqMaxFfn / 32 * 18;
 // Layout of one instantiation for token tiles of up to TOK tokens; DIQ: the
-// down weights are IQ4_NL (gate/up stay Q4_K).
-template <int TOK, bool DIQ = false>
+// down weights are IQ4_NL; GIQ: the gate/up weights too (decode tiles only).
+template <int TOK, bool DIQ = false, bool GIQ = false>
 struct Cfg {
+    static_assert(!GIQ || (DIQ && TOK <= 32), "IQ4_NL gate/up: with IQ4_NL down, decode tiles");
     // raw weight ring: a gate + up superblock, or (DIQ) a whole down tile
     static constexpr int kRawStage = DIQ ? kDiqRawStage : 2 * kSbBytes;
     static constexpr int kRawStages = (DIQ && TOK > 32) ? 2 : 3;
@@ -90,7 +91,7 @@ struct Cfg {
     // K=16 MMA per matrix, A'' = dmin*m_g*2^8 split hi/lo (exact in 22 bits), B'' =
     // the 8 group sums of x*s/32 split hi/lo, accumulated over the whole item in
     // D2 (read once per item) instead of per-superblock epilogue arithmetic.
-    static constexpr bool kMinD2 = TOK == kTcTokSmall;
+    static constexpr bool kMinD2 = TOK == kTcTokSmall && !GIQ;
     static constexpr int kBBytes = 2 * TOK * 128;             // B: TOK hi rows, then TOK lo rows, 128 B each
     static constexpr int kB2Bytes = kMinD2 ? 64 * TOK : 0;    // B'': two K halves x [hi rows | lo rows] x 16 B
     static constexpr int kBSlot = (kBBytes + kB2Bytes + 1023) & ~1023;
@@ -102,13 +103,16 @@ struct Cfg {
                          kOffV = kOffSc + 4 * kScSlot, kSmem = kOffV + kVBytes;
     // Tensor memory (512 columns): D[db][m] at (db*2+m)*kDCols; with the min term
     // D2[m] at kD2Col + m*kDCols and A''[buf][m] (8 columns) at kA2Col +
-    // (buf*2+m)*8; A[ab][m] (32 columns = 64 fp16 of one 64-value chunk) at
-    // kACol0 + (ab*2+m)*32.
+    // (buf*2+m)*8; A stage ab at kACol0 + ab*kAStride, its 32-column blocks (64
+    // fp16 of one 64-value chunk) at (m*2+p)*32 for matrix m and plane p (an
+    // IQ4_NL gate/up stage holds both planes of both matrices; a Q4_K stage
+    // matrix m at m*32; an IQ4_NL down stage plane p at p*32).
     static constexpr int kDCols = 2 * TOK;
     static constexpr int kD2Col = 4 * kDCols, kA2Col = kD2Col + 2 * kDCols;
     static constexpr int kACol0 = kMinD2 ? kA2Col + 32 : 4 * kDCols;
-    static constexpr int kAStages = (512 - kACol0) / 64 >= 4 ? 4 : (512 - kACol0) / 64;
-    static_assert(kAStages >= 2 && kACol0 + kAStages * 64 <= 512, "tensor memory budget");
+    static constexpr int kAStride = GIQ ? 128 : 64;
+    static constexpr int kAStages = (512 - kACol0) / kAStride >= 4 ? 4 : (512 - kACol0) / kAStride;
+    static_assert(kAStages >= 2 && kACol0 + kAStages * kAStride <= 512, "tensor memory budget");
     static_assert(kSmem % 16 == 0 && kScSlot % 16 == 0 && kOffB % 1024 == 0 && kBBytes % 1024 == 0 &&
                       kBSlot % 1024 == 0 && (TOK * 128) % 1024 == 0 && (16 * TOK) % 128 == 0, "alignment");
     // 227 KB per CTA, less about 4 KB of static shared memory (barriers, tables)
@@ -387,13 +391,13 @@ struct __align__(16) TokTab {
     int ex[TOK];    // expected contributions of the token (down; combine counting)
 };
 
-template <int TOK, bool DIQ>
+template <int TOK, bool DIQ, bool GIQ>
 __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a, const __grid_constant__ TcMaps maps) {
-    using C = Cfg<TOK, DIQ>;
+    using C = Cfg<TOK, DIQ, GIQ>;
     constexpr int kTok = TOK, kBBytes = C::kBBytes, kScXs = C::kScXs, kScSlot = C::kScSlot, kOffB = C::kOffB,
                   kOffSc = C::kOffSc, kOffV = C::kOffV, kDCols = C::kDCols, kACol0 = C::kACol0,
                   kAStages = C::kAStages, kBStages = C::kBStages, kRawStage = C::kRawStage,
-                  kRawStages = C::kRawStages;
+                  kRawStages = C::kRawStages, kAStride = C::kAStride;
     extern __shared__ __align__(1024) unsigned char smem[];
     __shared__ Bars bars;
     __shared__ Item items[4];
@@ -576,13 +580,14 @@ __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a,
                         if (!(ok = wait_phase(&bars.b_full[bs], (gch / kBStages) & 1, &abort_flag, err))) break;
                         if (gu || (c >> 1) == mi) {
                             tc_fence_after();
-                            const uint32_t ac = tmem + (uint32_t)(kACol0 + (ab * 2 + (gu ? mi : 0)) * 32);
+                            const uint32_t ac =
+                                tmem + (uint32_t)(kACol0 + ab * kAStride + (gu ? mi * (GIQ ? 64 : 32) : 0));
                             const uint64_t bd = b_desc0 + (uint64_t)((bs * C::kBSlot) >> 4);
                             mma_ts(d, ac, bd, idesc, gu ? c != 0 : (c & 1) != 0);
                             mma_ts1(d, ac + 8, bd + 2, idesc);
                             mma_ts1(d, ac + 16, bd + 4, idesc);
                             mma_ts1(d, ac + 24, bd + 6, idesc);
-                            if (DIQ && !gu) {  // IQ4_NL down: the lo plane of A into the same D
+                            if (gu ? GIQ : DIQ) {  // IQ4_NL: the lo plane of A into the same D
                                 mma_ts1(d, ac + 32, bd, idesc);
                                 mma_ts1(d, ac + 40, bd + 2, idesc);
                                 mma_ts1(d, ac + 48, bd + 4, idesc);
@@ -725,7 +730,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a,
                 // row scales: matrix nib (gate by the low-nibble warps, up by the high-nibble ones)
                 if (gsb >= 4 && !(ok = wait_phase(&bars.sc_empty[sc_slot], ((gsb >> 2) - 1) & 1, &abort_flag, err)))
                     break;
-                if (nib < mats && !diq) {
+                if (nib < mats && !diq && !GIQ) {
                     uint4 *scs = reinterpret_cast<uint4 *>(smem + kOffSc + sc_slot * kScSlot);
                     scs[nib * kTcRows + ct] = q4k_row_scales(raw + nib * kSbBytes + ct * 144);
                 }
@@ -749,13 +754,20 @@ __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a,
                         if (DIQ && diq) {  // block 2*chunk + nib of the row: hi plane, lo plane
                             uint32_t rh[16], rl[16];
                             iq4_block_cols(raw + ct * a.drb + (size_t)(2 * (4 * sb + c + h) + nib) * 18, rh, rl);
-                            tmem_st16(a_lanes + (uint32_t)((ab * 2) * 32), rh);
-                            tmem_st16(a_lanes + (uint32_t)((ab * 2 + 1) * 32), rl);
+                            tmem_st16(a_lanes + (uint32_t)(ab * kAStride), rh);
+                            tmem_st16(a_lanes + (uint32_t)(ab * kAStride + 32), rl);
+                        } else if (GIQ) {  // gate/up: block 2*chunk + nib of each matrix's row (144 B per 8 blocks)
+                            for (int m = 0; m < 2; m++) {
+                                uint32_t rh[16], rl[16];
+                                iq4_block_cols(raw + m * kSbBytes + ct * 144 + (2 * (c + h) + nib) * 18, rh, rl);
+                                tmem_st16(a_lanes + (uint32_t)(ab * kAStride + m * 64), rh);
+                                tmem_st16(a_lanes + (uint32_t)(ab * kAStride + m * 64 + 32), rl);
+                            }
                         } else {
                             for (int m = 0; m < mats; m++) {
                                 uint32_t r[16];
                                 q4k_half_cols(raw + m * kSbBytes + ct * 144, c + h, nib, r);
-                                tmem_st16(a_lanes + (uint32_t)((ab * 2 + m) * 32), r);
+                                tmem_st16(a_lanes + (uint32_t)(ab * kAStride + m * 32), r);
                             }
                         }
                     }
@@ -913,6 +925,40 @@ __global__ void __launch_bounds__(kThreads, 1) tc_experts_kernel(const TcArgs a,
                                     acc2[cb * 8 + i] = __fmaf_rn(
                                         dsc, __fmaf_rn(__uint_as_float(rl[i]), 1.0f / 2048.0f, __uint_as_float(rh[i])),
                                         acc2[cb * 8 + i]);
+                            }
+                        }
+                    }
+                } else if (GIQ && gu) {
+                    // IQ4_NL gate/up: the block scales are in A; only the token's B scale
+#pragma unroll
+                    for (int m = 0; m < 2; m++) {
+                        const uint32_t col0 = lanes + (uint32_t)((db * 2 + m) * kDCols);
+#pragma unroll
+                        for (int cb = 0; cb < kHalf / 8; cb++) {
+                            if (cb * 8 >= hw) break;
+                            uint32_t rh[8], rl[8];
+                            if (by_tok) {  // gather the slots' token columns
+#pragma unroll
+                                for (int i = 0; i < 8; i++) {
+                                    const int c = tb.tok[min(j0 + cb * 8 + i, it.n - 1)];
+                                    rh[i] = tmem_ld1(col0 + c);
+                                    rl[i] = tmem_ld1(col0 + kTok + c);
+                                }
+                            } else {
+                                tmem_ld8_nw(col0 + j0 + cb * 8, rh);
+                                tmem_ld8_nw(col0 + kTok + j0 + cb * 8, rl);
+                            }
+                            tmem_wait_ld();
+#pragma unroll
+                            for (int pp = 0; pp < 4; pp++) {
+                                if (cb * 8 + 2 * pp >= hw) break;
+                                const int j = j0 + cb * 8 + 2 * pp;
+                                const int c0 = by_tok ? tb.tok[min(j, it.n - 1)] : j;
+                                const int c1 = by_tok ? tb.tok[min(j + 1, it.n - 1)] : j + 1;
+                                const float2 hi = make_float2(__uint_as_float(rh[2 * pp]), __uint_as_float(rh[2 * pp + 1]));
+                                const float2 lo = make_float2(__uint_as_float(rl[2 * pp]), __uint_as_float(rl[2 * pp + 1]));
+                                float2 &ac = acc[m][cb * 4 + pp];
+                                ac = __ffma2_rn(__ffma2_rn(lo, k2048, hi), make_float2(inv4[c0 * 4], inv4[c1 * 4]), ac);
                             }
                         }
                     }
@@ -1351,10 +1397,11 @@ int sm_count_tc() {
 
 namespace nb {
 
-bool tc_supported(int H, int F, int QG, int QD) {
-    if (QG != 12 || H % 256 || H < 256 || F % kTcRows || F < kTcRows || encoder() == nullptr) return false;
-    if (QD == 12) return F % 256 == 0;
-    return QD == 20 && F <= kDiqMaxFfn;
+bool tc_supported(int H, int F, int QG, int QD, int max_tile) {
+    if (H % 256 || H < 256 || F % kTcRows || F < kTcRows || encoder() == nullptr) return false;
+    if (QG == 12 && QD == 12) return F % 256 == 0;
+    if (QG == 12 && QD == 20) return F <= kDiqMaxFfn;
+    return QG == 20 && QD == 20 && F <= kDiqMaxFfn && max_tile <= kTokDecode;
 }
 
 int tc_make_maps(const TcArgs &a, TcMaps &m, int tok) {
@@ -1391,17 +1438,17 @@ int tc_make_maps(const TcArgs &a, TcMaps &m, int tok) {
     if (!rc && a.xs16) rc = make_map_2d(&m.gx_hi, f16, 2, a.xs16, H / 32, xrows, H / 8, 8, tok, none);
     if (!rc && a.xs16) rc = make_map_2d(&m.gx_lo, f16, 2, a.xs16 + H / 32, H / 32, xrows, H / 8, 8, tok, none);
     if (!rc && !a.xs16) m.gx_hi = m.gx_lo = m.sx;
-    if (!rc && tok == kTcTokSmall && !a.xs16) rc = cudaErrorInvalidValue;  // the min term needs the fp16 group sums
+    if (!rc && tok == kTcTokSmall && !a.gu_iq4 && !a.xs16) rc = cudaErrorInvalidValue;  // the min term needs the fp16 group sums
     if (!rc) rc = make_map_2d(&m.sm, f32, 4, a.msum, F / 32, rows, F / 8, 8, tok, none);
     if (!rc) rc = make_map_2d(&m.ix, f32, 4, a.xinv, 4, xrows, 16, 4, tok, none);
     if (!rc) rc = make_map_2d(&m.im, f32, 4, a.midinv, a.mi_stride, rows, 4 * (size_t)a.mi_stride, 4, tok, none);
     return rc;
 }
 
-template <int TOK, bool DIQ>
+template <int TOK, bool DIQ, bool GIQ>
 int tc_launch_tok(const TcArgs &a, const TcMaps &m, cudaStream_t st, bool pdl) {
-    constexpr int smem = Cfg<TOK, DIQ>::kSmem;
-    int rc = cudaFuncSetAttribute(tc_experts_kernel<TOK, DIQ>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    constexpr int smem = Cfg<TOK, DIQ, GIQ>::kSmem;
+    int rc = cudaFuncSetAttribute(tc_experts_kernel<TOK, DIQ, GIQ>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (rc) return rc;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(sm_count_tc());
@@ -1413,18 +1460,24 @@ int tc_launch_tok(const TcArgs &a, const TcMaps &m, cudaStream_t st, bool pdl) {
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, tc_experts_kernel<TOK, DIQ>, a, m);
+    return cudaLaunchKernelEx(&cfg, tc_experts_kernel<TOK, DIQ, GIQ>, a, m);
 }
 
 template <bool DIQ>
 int tc_launch_fmt(const TcArgs &a, const TcMaps &m, cudaStream_t st, bool pdl, int max_tile) {
-    if (max_tile <= kTcTokSmall) return tc_launch_tok<kTcTokSmall, DIQ>(a, m, st, pdl);
-    if (max_tile <= kTokDecode) return tc_launch_tok<kTokDecode, DIQ>(a, m, st, pdl);
-    if (max_tile <= kTcTok) return tc_launch_tok<kTcTok, DIQ>(a, m, st, pdl);
+    if (max_tile <= kTcTokSmall) return tc_launch_tok<kTcTokSmall, DIQ, false>(a, m, st, pdl);
+    if (max_tile <= kTokDecode) return tc_launch_tok<kTokDecode, DIQ, false>(a, m, st, pdl);
+    if (max_tile <= kTcTok) return tc_launch_tok<kTcTok, DIQ, false>(a, m, st, pdl);
     return cudaErrorInvalidValue;
 }
 
 int tc_launch(const TcArgs &a, const TcMaps &m, cudaStream_t st, bool pdl, int max_tile) {
+    if (a.gu_iq4) {  // IQ4_NL gate/up and down: decode tiles only
+        if (!a.dn_iq4) return cudaErrorInvalidValue;
+        if (max_tile <= kTcTokSmall) return tc_launch_tok<kTcTokSmall, true, true>(a, m, st, pdl);
+        if (max_tile <= kTokDecode) return tc_launch_tok<kTokDecode, true, true>(a, m, st, pdl);
+        return cudaErrorInvalidValue;
+    }
     return a.dn_iq4 ? tc_launch_fmt<true>(a, m, st, pdl, max_tile) : tc_launch_fmt<false>(a, m, st, pdl, max_tile);
 }
 

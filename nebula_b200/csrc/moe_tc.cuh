@@ -1,4 +1,4 @@
-// Tensor-core (tcgen05) expert kernel for Q4_K experts (IQ4_NL down allowed): interface.
+// Tensor-core (tcgen05) expert kernel for Q4_K and IQ4_NL experts: interface.
 #pragma once
 #include <cuda.h>
 #include "common.cuh"
@@ -19,11 +19,12 @@ struct SubJob {
 
 struct TcArgs {
     int T, H, F;
-    // Q4_K gate/up rows of H values; down rows of F values, Q4_K or (dn_iq4)
-    // IQ4_NL; the shared expert (sg/su/sd) in the same formats
+    // gate/up rows of H values, Q4_K or (gu_iq4, decode tiles, with IQ4_NL
+    // down) IQ4_NL; down rows of F values, Q4_K or (dn_iq4) IQ4_NL; the shared
+    // expert (sg/su/sd) in the same formats
     const unsigned char *gate, *up, *down, *sg, *su, *sd;
     size_t grb, drb;
-    int dn_iq4;
+    int gu_iq4, dn_iq4;
     // Gate/up activations: either per token (all_tok = 1: every gate/up tile
     // multiplies all T <= tile tokens and keeps its own columns) or per routed
     // row (rows as for the SwiGLU outputs below, filled by tc_prep_rows_launch).
@@ -88,8 +89,9 @@ struct TcMaps {
 };
 
 // Q4_K gate/up (hidden a multiple of 256, ffn of 128) with Q4_K down (ffn a
-// multiple of 256) or IQ4_NL down (ffn up to 640).
-bool tc_supported(int H, int F, int QG, int QD);
+// multiple of 256) or IQ4_NL down (ffn up to 640); IQ4_NL gate/up with IQ4_NL
+// down for launches whose token tiles are at most 32 (decode).
+bool tc_supported(int H, int F, int QG, int QD, int max_tile = kTcTok);
 int tc_make_maps(const TcArgs &a, TcMaps &m, int max_tile);
 // max_tile: the largest token tile of the launch (sub-jobs, and the split of
 // the shared expert's tokens: shared sub-job i covers tokens i*max_tile ..).

@@ -80,7 +80,7 @@ def q4k_2048(L):
 
 @pytest.fixture(scope="module")
 def iq4_2048(L):
-    return Layer(L, 2048, 512, 20, 20, seed=1)
+    return Layer(L, 2048, 512, 20, 20, seed=1, shared=True)
 
 
 @pytest.fixture(scope="module")
@@ -113,6 +113,22 @@ def test_routed_iq4nl_2048(L, ref2048, iq4_2048, T):
     ids, w = random_routes(rng, T)
     out, _ = iq4_2048.routed(x, ids, w)
     assert_parity(out, oracle_routed(ref2048, iq4_2048, x, ids, w), f"IQ4_NL T={T}")
+
+
+@pytest.mark.parametrize("T", (1, 17, 30, 33))
+def test_layer_iq4nl_with_shared_expert(L, ref2048, restate, iq4_2048, T):
+    """All-IQ4_NL experts (config 2's format) through the whole layer with an
+    IQ4_NL shared expert: 24- and 32-token decode tiles on the tensor cores, and
+    a batch above 32 on the general path."""
+    rng = np.random.default_rng(500 + T)
+    x = rng.normal(0, 1, (T, 2048)).astype(np.float32)
+    out, ids, w, ws = iq4_2048.layer(x)
+    e_out, e_ids, e_w, _ = orc.moe_layer(ref2048, restate, x, iq4_2048.hrouter, iq4_2048.hgate, 20,
+                                         iq4_2048.hup, 20, iq4_2048.hdown, 20, shared=iq4_2048.shared)
+    np.testing.assert_array_equal(ids, e_ids)
+    assert_parity(out, e_out, f"IQ4_NL layer T={T}")
+    inv, sel, used = L.status(ws)
+    assert inv == 0 and sel == T * 10 and used == len(np.unique(e_ids))
 
 
 @pytest.mark.parametrize("T", (1, 5, 17, 33))
