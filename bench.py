@@ -107,8 +107,9 @@ def traffic_per_launch(kernel: str, workload: str, alg_bytes: float) -> tuple[fl
     for line in p.read_text().splitlines():
         f = line.split()
         if len(f) >= 3 and not line.startswith("#") and f[0] == kernel and f[1] == workload:
-            return float(f[2]) * alg_bytes, ("ncu dram__bytes_read.sum + dram__bytes_write.sum, 2-layer capture, "
-                                             f"{float(f[2]):.4f} x the algorithmic bytes (profiles/traffic.txt)")
+            return float(f[2]) * alg_bytes, ("ncu dram__bytes_read.sum + dram__bytes_write.sum of one capture, "
+                                             f"{float(f[2]):.4f} x the algorithmic bytes (profiles/traffic.txt: "
+                                             f"{' '.join(f[3:])})")
     return None, None
 
 
@@ -472,7 +473,7 @@ def read_profile(L) -> dict:
 
 
 def single_layer_config(torch, L, peaks, T: int, h: int, f: int, gt: int, dt: int, shared: bool, seed0: int,
-                        cpu: bool, cpu_seconds: float, what: str, steps: int) -> dict:
+                        cpu: bool, cpu_seconds: float, what: str, steps: int, traffic_key=None) -> dict:
     """One routed-MoE layer at T tokens, timed over ROT rotated layers (graph replay),
     with its roofline and the reference CPU MoE on the same bytes."""
     st = Stack(L, ROT, T, seed0=seed0, h=h, f=f, gt=gt, dt=dt, shared=shared, bias=False)
@@ -504,6 +505,9 @@ def single_layer_config(torch, L, peaks, T: int, h: int, f: int, gt: int, dt: in
                         "algorithmic_bytes_per_launch": kbytes,
                         "phase_ms_per_launch": {k: v[0] / v[1] for k, v in prof.items() if v[1]}},
            "l2": f"{ROT} rotated layers ({ROT * E * eb / 1e9:.1f} GB of experts)"}
+    if traffic_key and kern == "experts":
+        tr, src = traffic_per_launch(*traffic_key, kbytes)
+        res["roofline"]["traffic"], res["roofline"]["traffic_source"] = tr, src
     if cpu:
         cores = host_cores()
         hl = HostLayers(T, seed0=seed0, h=h, f=f, gt=gt, dt=dt, shared=shared, bias=False)
@@ -826,14 +830,16 @@ def main() -> None:
         want_cpu = not args.no_cpu
         configs["config1"] = single_layer_config(
             torch, L, peaks, 4, H, F, Q4K, Q4K, False, 11, want_cpu, 3.0,
-            "config 1: 1 layer, T=4, 512 Q4_K experts, router -> top-10, routed only", args.steps)
+            "config 1: 1 layer, T=4, 512 Q4_K experts, router -> top-10, routed only", args.steps,
+            ("tc_experts_kernel<24>", "T17"))
         configs["config2"] = single_layer_config(
             torch, L, peaks, 17, H, F, IQ4NL, IQ4NL, False, 12, want_cpu, 3.0,
-            "config 2: 1 layer, T=17, 512 IQ4_NL experts, router -> top-10, routed only", args.steps)
+            "config 2: 1 layer, T=17, 512 IQ4_NL experts, router -> top-10, routed only", args.steps,
+            ("tc_experts_kernel<24,1,1>", "config2-T17"))
         configs["product"] = single_layer_config(
             torch, L, peaks, 17, 2560, 640, Q4K, IQ4NL, True, 13, want_cpu, 3.0,
             "product shape: 1 layer, T=17, hidden 2560 / FFN 640, Q4_K gate/up + IQ4_NL down, router + shared "
-            "expert", args.steps)
+            "expert", args.steps, ("tc_experts_kernel<24,1,0>", "product-T17"))
         configs["product_prefill"] = prefill_product(torch, L, peaks, want_cpu, 4.0, args.steps)
         sweep = {}
         for t in range(1, T + 1):

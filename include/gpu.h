@@ -185,7 +185,8 @@ int qg_moe_layer(float *out, int *ids_out, float *weights_out, const float *x, i
  * every rank; a rank that stops makes the others' combines time out after
  * 2 s (error bit 8: qg_moe_status returns cudaErrorLaunchTimeout) with NaN
  * output rows instead of hanging; every rank then zeroes its workspace
- * before the next call. Q4_K only.
+ * before the next call. Q4_K gate/up with Q4_K or IQ4_NL down (the shared
+ * expert in the same formats).
  * Large batches (tokens > 32): rank r owns tokens [r*B, (r+1)*B) with
  * B = ceil(tokens / ranks); each rank computes the router logits and top-10
  * of its own tokens and sends their ids and weights to every rank (ids_out

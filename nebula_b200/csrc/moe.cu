@@ -1546,9 +1546,10 @@ extern "C" int qg_moe_layer_ep(float *out, int *ids_out, float *weights_out, con
         n_local < 1 || n_local > kExperts)
         return cudaErrorInvalidValue;
     const bool large = tokens > kMaxDecodeTokens;
-    if (gt != 12 || ut != 12 || dt != 12 || (sg && (sgt != 12 || sut != 12 || sdt != 12)) ||
+    // the tensor-core path: Q4_K gate/up, Q4_K or IQ4_NL down (the shared expert alike)
+    if (gt != 12 || ut != 12 || (dt != 12 && dt != 20) || (sg && (sgt != 12 || sut != 12 || sdt != dt)) ||
         (!large && !dec_supported(tokens, hidden, ffn, gt, dt)) || !tc_supported(hidden, ffn, gt, dt))
-        return cudaErrorNotSupported;  // expert parallelism runs on the Q4_K tensor-core path
+        return cudaErrorNotSupported;
     void *workspace = workspaces[rank];
     for (int p = 0; p < ranks; p++)
         if (!workspaces[p]) return cudaErrorInvalidValue;

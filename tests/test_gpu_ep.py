@@ -30,7 +30,6 @@ import torch.multiprocessing as mp
 pytestmark = pytest.mark.gpu
 
 H, F = 2048, 512
-QROW_H, QROW_F = H // 256 * 144, F // 256 * 144  # Q4_K row bytes
 TIMEOUT = 702  # cudaErrorLaunchTimeout, as qg_moe_status reports a bounded wait that ran out
 
 
@@ -41,15 +40,16 @@ def _free_port():
 
 
 class _Rank:
-    """One rank's layer: full weights (for the single-GPU reference) and its own experts."""
+    """One rank's layer: full weights (for the single-GPU reference) and its own experts.
+    Q4_K gate/up; down (and the shared down) Q4_K or IQ4_NL (dt = 20)."""
 
-    def __init__(self, L, ep, rank, world):
-        self.L, self.rank, self.world = L, rank, world
-        self.gate, self.up = L.synth_weights(12, 512 * F, H, 901), L.synth_weights(12, 512 * F, H, 902)
-        self.down = L.synth_weights(12, 512 * H, F, 903)
-        self.router = L.synth_weights(0, 512, H, 904)
-        self.sg, self.su = L.synth_weights(12, F, H, 905), L.synth_weights(12, F, H, 906)
-        self.sd, self.sr = L.synth_weights(12, H, F, 907), L.synth_weights(0, 1, H, 908)
+    def __init__(self, L, ep, rank, world, h=H, f=F, dt=12):
+        self.L, self.rank, self.world, self.h, self.f, self.dt = L, rank, world, h, f, dt
+        self.gate, self.up = L.synth_weights(12, 512 * f, h, 901), L.synth_weights(12, 512 * f, h, 902)
+        self.down = L.synth_weights(dt, 512 * h, f, 903)
+        self.router = L.synth_weights(0, 512, h, 904)
+        self.sg, self.su = L.synth_weights(12, f, h, 905), L.synth_weights(12, f, h, 906)
+        self.sd, self.sr = L.synth_weights(dt, h, f, 907), L.synth_weights(0, 1, h, 908)
         ranking = np.random.default_rng(11).permutation(512)
         bias = np.zeros(512, np.float32)
         bias[ranking] = (-1.1 * np.log(np.arange(1, 513))).astype(np.float32)
@@ -57,26 +57,26 @@ class _Rank:
         owner = ep.snake_owner(ranking, world)
         loc, experts = ep.local_map(owner, rank)
         self.n_local = len(experts)
-        self.lgate = ep.extract_experts(self.gate, experts, F, QROW_H)
-        self.lup = ep.extract_experts(self.up, experts, F, QROW_H)
-        self.ldown = ep.extract_experts(self.down, experts, H, QROW_F)
+        self.lgate = ep.extract_experts(self.gate, experts, f, L.row_bytes(12, h))
+        self.lup = ep.extract_experts(self.up, experts, f, L.row_bytes(12, h))
+        self.ldown = ep.extract_experts(self.down, experts, h, L.row_bytes(dt, f))
         self.loc = L.Device(loc)
 
     def single(self, x, T, ws):
-        L = self.L
-        ref = L.Device.empty((T, H), np.float32)
+        L, dt = self.L, self.dt
+        ref = L.Device.empty((T, self.h), np.float32)
         rid = L.Device.empty((T, 10), np.int32)
         L.call("moe_layer", ref.p, rid.p, None, x.p, T, self.router.p, self.bias.p, self.gate.p, 12, self.up.p, 12,
-               self.down.p, 12, self.sg.p, 12, self.su.p, 12, self.sd.p, 12, self.sr.p, H, F, ws.p)
+               self.down.p, dt, self.sg.p, 12, self.su.p, 12, self.sd.p, dt, self.sr.p, self.h, self.f, ws.p)
         return ref.get(), rid.get()
 
     def ep_call(self, x, T, grp, shared_rank):
-        L = self.L
-        out = L.Device.empty((T, H), np.float32)
+        L, dt = self.L, self.dt
+        out = L.Device.empty((T, self.h), np.float32)
         eid = L.Device.empty((T, 10), np.int32)
         L.call("moe_layer_ep", out.p, eid.p, None, x.p, T, self.router.p, self.bias.p, self.lgate.p, 12, self.lup.p,
-               12, self.ldown.p, 12, self.n_local, self.loc.p, self.sg.p, 12, self.su.p, 12, self.sd.p, 12,
-               self.sr.p, shared_rank, H, F, self.rank, self.world, grp.ptrs)
+               12, self.ldown.p, dt, self.n_local, self.loc.p, self.sg.p, 12, self.su.p, 12, self.sd.p, dt,
+               self.sr.p, shared_rank, self.h, self.f, self.rank, self.world, grp.ptrs)
         return out, eid
 
     def check(self, x, T, grp, ws, call, shared_rank):
@@ -98,9 +98,9 @@ class _Rank:
         return errors
 
 
-def _x(T, seed):
+def _x(T, seed, h=H):
     from nebula_b200 import lib as L
-    return L.Device(np.random.default_rng(seed).normal(0, 1, (T, H)).astype(np.float32))
+    return L.Device(np.random.default_rng(seed).normal(0, 1, (T, h)).astype(np.float32))
 
 
 def _status(L, ws):
@@ -119,8 +119,15 @@ def _worker(rank, world, port, results, scenario, T):
         from nebula_b200 import ep
         from nebula_b200 import lib as L
         L.load()
-        lay = _Rank(L, ep, rank, world)
         errors = []
+        if scenario == "product":  # Nebula's mix: Q4_K gate/up, IQ4_NL down, 2560/640
+            lay = _Rank(L, ep, rank, world, 2560, 640, 20)
+            grp = ep.EpGroup(T, 2560, 640, rank, world)
+            ws = L.workspace(T, 2560, 640)
+            for call in range(3):
+                errors += lay.check(_x(T, 400 + call, 2560), T, grp, ws, call, call % world)
+        else:
+            lay = _Rank(L, ep, rank, world)
         if scenario == "parity":
             grp = ep.EpGroup(T, H, F, rank, world)
             ws = L.workspace(T, H, F)
@@ -180,6 +187,12 @@ def _run(scenario, T):
 @pytest.mark.parametrize("T", (17, 100, 2048))
 def test_expert_parallel_matches_single_gpu(T):
     _run("parity", T)
+
+
+@pytest.mark.parametrize("T", (17, 100))
+def test_expert_parallel_product_mix(T):
+    """Q4_K gate/up with IQ4_NL down at hidden 2560 / ffn 640, decode and large batches."""
+    _run("product", T)
 
 
 def test_expert_parallel_one_workspace_changing_sizes():
