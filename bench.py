@@ -62,7 +62,7 @@ RANKING = ROOT / "tests" / "golden" / "expert_ranking.npz"
 
 
 def row_bytes(typ: int, cols: int) -> int:
-    return {0: cols * 4, Q4K: cols // 256 * 144, IQ4NL: cols // 32 * 18}[typ]
+    return {0: cols * 4, 8: cols // 32 * 34, 14: cols // 256 * 210, Q4K: cols // 256 * 144, IQ4NL: cols // 32 * 18}[typ]
 
 
 def expert_bytes(h: int, f: int, gt: int, dt: int) -> int:
@@ -525,6 +525,66 @@ def single_layer_config(torch, L, peaks, T: int, h: int, f: int, gt: int, dt: in
     return res
 
 
+def dense_blocks(typ: int, rows: int, cols: int, seed: int) -> np.ndarray:
+    """Random Q8_0 (8) or Q6_K (14) rows with valid fp16 scales (the device generator
+    covers F32, Q4_K and IQ4_NL)."""
+    rng = np.random.default_rng(seed)
+    rb = row_bytes(typ, cols)
+    w = rng.integers(0, 256, rows * rb, dtype=np.uint8)
+    blk, d_off = (34, 0) if typ == 8 else (210, 208)
+    b = w.reshape(-1, blk)
+    b[:, d_off:d_off + 2] = np.frombuffer(np.full(len(b), 0.001, np.float16).tobytes(), np.uint8).reshape(-1, 2)
+    return w
+
+
+def dense_gemv(torch, L, peaks, cpu: bool, steps: int) -> dict:
+    """qg_matmul (the dense dequant GEMV that serves every non-MoE projection) on an 8192 x 2560
+    projection in five formats at T = 1 and 17, rotated over copies that exceed L2, with its HBM
+    roofline and a bitwise check against the reference qc_matmul."""
+    rows, cols = 8192, 2560
+    res = {"workload": f"qg_matmul, {rows} x {cols} weights, T = 1 and 17, rotated copies > 300 MB (past L2), "
+                       "one CUDA graph of all copies' launches per timed step"}
+    ref = None
+    if cpu:
+        from oracle import oracle as orc
+        ref = orc.RefCPU(2560, 640)
+    for name, typ in (("f32", 0), ("q8_0", 8), ("q6_k", 14), ("q4_k", Q4K), ("iq4_nl", IQ4NL)):
+        mb = rows * row_bytes(typ, cols)
+        copies = max(2, -(-300_000_000 // mb))
+        if typ in (8, 14):
+            host = dense_blocks(typ, rows, cols, 40 + typ)
+            ws = [L.Device(host) for _ in range(copies)]
+        else:
+            ws = [L.synth_weights(typ, rows, cols, 40 + typ + i) for i in range(copies)]
+        line = {"copies": copies, "weight_bytes": mb}
+        for T in (1, 17):
+            x = L.synth_normal(T * cols, 77)
+            out = L.Device.empty((T, rows), np.float32)
+
+            L.call("matmul", out.p, ws[0].p, typ, rows, cols, x.p, T)  # eager first use (module load, attributes)
+            g = C.c_void_p()  # one graph of all copies' launches, so launch overhead is not timed
+            L.call("graph_begin", C.byref(g))
+            for w in ws:
+                L.call("matmul", out.p, w.p, typ, rows, cols, x.p, T)
+            L.call("graph_end", g)
+            for _ in range(3):
+                L.call("graph_launch", g)
+            ms = event_ms(torch, lambda: L.call("graph_launch", g), max(3, steps // 4)) / copies
+            L.load().qg_graph_destroy(g)
+            nbytes = mb + T * cols * 4 + T * rows * 4
+            line[f"T{T}"] = {"us": ms * 1e3, "gbs": nbytes / (ms / 1e3) / 1e9,
+                             "hbm_frac": nbytes / (ms / 1e3) / 1e9 / peaks["hbm_gbs"]}
+            if ref is not None and T == 17:
+                L.call("matmul", out.p, ws[0].p, typ, rows, cols, x.p, T)
+                hw = host if typ in (8, 14) else ws[0].get()
+                line["bitwise_vs_qc_matmul"] = bool(np.array_equal(
+                    out.get(), ref.matmul(hw, typ, rows, cols, x.get().reshape(T, cols))))
+        res[name] = line
+        del ws
+    L.call("sync")
+    return res
+
+
 def prefill_product(torch, L, peaks, cpu: bool, cpu_seconds: float, steps: int) -> dict:
     """Prefill of the production mix (hidden 2560 / FFN 640, Q4_K gate/up + IQ4_NL down): one
     layer at T=2048 routed from N(0,1) logits (about 40 tokens per expert), routed experts only,
@@ -841,6 +901,7 @@ def main() -> None:
             "product shape: 1 layer, T=17, hidden 2560 / FFN 640, Q4_K gate/up + IQ4_NL down, router + shared "
             "expert", args.steps, ("tc_experts_kernel<24,1,0>", "product-T17"))
         configs["product_prefill"] = prefill_product(torch, L, peaks, want_cpu, 4.0, args.steps)
+        configs["dense_gemv"] = dense_gemv(torch, L, peaks, want_cpu, args.steps)
         sweep = {}
         for t in range(1, T + 1):
             g = stack.capture(t)

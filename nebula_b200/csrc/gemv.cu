@@ -3,9 +3,11 @@
 //
 // qg_matmul keeps the reference's 32-lane accumulation order (lane j owns
 // columns j mod 32, then the 16/8/4/2/1 tree), so its output is bitwise equal
-// to qc_matmul (qwen/cpu.c:119-148): one warp per weight row, or for fp32 rows
-// against 64 or more tokens a tiled kernel with the same order per output. The router GEMV
-// that feeds top-10 selection relies on this for bit-exact expert ids.
+// to qc_matmul (qwen/cpu.c:119-148): a staged kernel (chunks of rows and token
+// vectors copied into shared memory, one warp per two rows), a tiled kernel
+// for fp32 rows against 64 or more tokens, and one warp per row for shapes
+// neither takes, all with the same order per output. The router GEMV that
+// feeds top-10 selection relies on this for bit-exact expert ids.
 #include "quant.cuh"
 
 using namespace nb;
@@ -131,12 +133,219 @@ __global__ void __launch_bounds__(kTR * kTT / 2) matmul_f32_tiled_kernel(float *
         }
 }
 
+// Staged GEMV for batches the tiled kernel does not take: a CTA of kGvWarps
+// warps owns kGvRows rows per warp. Each 256-column chunk of those rows and of
+// the token vectors is copied into shared memory (two stages: the next chunk's
+// copies are in flight while one is multiplied), so a chunk's loads
+// are all issued at once instead of one dependent load per lane step. Lane j then
+// multiplies columns j, j+32, ... of the chunk in increasing order with one
+// fused multiply-add per element, continuing the same per-lane sums across
+// chunks: the order of matmul_kernel, so the results are bitwise the same.
+constexpr int kGvWarps = 8, kGvRows = 2, kGvK = 256;
+constexpr int kGvRowsCta = kGvWarps * kGvRows;
+
+__device__ __forceinline__ void cp_async4(void *dst, const void *src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src)
+                 : "memory");
+}
+
+// Lane columns of one staged chunk of rows r0..r0+nr-1 (row r's bytes at
+// rows + r*pitch) against n token vectors xs[t][kGvK]: acc[r][t] += w * x in
+// increasing column order. T >= 0: that format; T < 0: `type`, per element.
+template <int T, int NT>
+__device__ __forceinline__ void gv_chunk(const unsigned char *rows, int pitch, int nr, int type, const float *xs,
+                                         int kn, int n, const float *lut, float2 *gv_scales,
+                                         float (&acc)[kGvRows][NT]) {
+    const int lane = threadIdx.x & 31;
+    if (T == 12) {  // one Q4_K superblock per chunk (kn = 256)
+        // (d*sc, -dmin*m) of the 8 sub-blocks of each row, decoded by lanes 0..7 and
+        // read back as broadcasts; nibbles become exact floats through the exponent
+        // field (q + 2^23 - 2^23); w = d*sc*q - dmin*m with one rounding, in pairs
+        float2 *scl = gv_scales + (threadIdx.x >> 5) * (kGvRows * 8);
+#pragma unroll
+        for (int r = 0; r < kGvRows; r++) {
+            if (r < nr && lane < 8) {
+                const unsigned char *p = rows + r * pitch;
+                int s, m;
+                k_scale_min(p + 4, lane, s, m);
+                scl[r * 8 + lane] = make_float2(half_at(p) * static_cast<float>(s),
+                                                -(half_at(p + 2) * static_cast<float>(m)));
+            }
+        }
+        __syncwarp();
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const int k0 = 64 * i + lane;  // sub-block 2i; sub-block 2i+1 at k0 + 32
+            float x0[NT], x1[NT];
+#pragma unroll
+            for (int t = 0; t < NT; t++) {
+                x0[t] = t < n ? xs[t * kGvK + k0] : 0.0f;
+                x1[t] = t < n ? xs[t * kGvK + k0 + 32] : 0.0f;
+            }
+#pragma unroll
+            for (int r = 0; r < kGvRows; r++) {
+                if (r < nr) {
+                    const float4 sc = *reinterpret_cast<const float4 *>(scl + r * 8 + 2 * i);  // ds0, -dm0, ds1, -dm1
+                    const unsigned b = rows[r * pitch + 16 + 32 * i + lane];
+                    const float2 q = __fadd2_rn(make_float2(__uint_as_float((b & 15u) | 0x4B000000u),
+                                                            __uint_as_float((b >> 4) | 0x4B000000u)),
+                                                make_float2(-8388608.0f, -8388608.0f));
+                    const float2 wv = __ffma2_rn(make_float2(sc.x, sc.z), q, make_float2(sc.y, sc.w));
+#pragma unroll
+                    for (int t = 0; t < NT; t++)
+                        if (t < n) acc[r][t] = __fmaf_rn(wv.x, x0[t], acc[r][t]);
+#pragma unroll
+                    for (int t = 0; t < NT; t++)
+                        if (t < n) acc[r][t] = __fmaf_rn(wv.y, x1[t], acc[r][t]);
+                }
+            }
+        }
+        __syncwarp();  // the scales are rewritten for the next chunk
+        return;
+    }
+    for (int m = 0; m < kn / 32; m++) {
+        const int k = 32 * m + lane;
+        float xv[NT];
+#pragma unroll
+        for (int t = 0; t < NT; t++) xv[t] = t < n ? xs[t * kGvK + k] : 0.0f;
+#pragma unroll
+        for (int r = 0; r < kGvRows; r++) {
+            if (r >= nr) break;
+            const unsigned char *p = rows + r * pitch;
+            float a;
+            if (T == 0) {
+                a = reinterpret_cast<const float *>(p)[k];
+            } else if (T == 8) {  // Q8_0: 34-byte blocks, the lane's value is byte 2 + lane
+                const unsigned char *b = p + m * 34;
+                a = half_at(b) * static_cast<float>(reinterpret_cast<const signed char *>(b + 2)[lane]);
+            } else if (T == 20) {  // IQ4_NL: 18-byte blocks
+                const unsigned char *b = p + m * 18;
+                const unsigned q = b[2 + (lane & 15)];
+                a = half_at(b) * lut[lane < 16 ? (q & 15) : (q >> 4)];
+            } else {
+                a = decode_at(p, T < 0 ? type : T, k);
+            }
+#pragma unroll
+            for (int t = 0; t < NT; t++)
+                if (t < n) acc[r][t] = __fmaf_rn(a, xv[t], acc[r][t]);
+        }
+    }
+}
+
+// cb / cb_tail: bytes of a row's full chunk and of its last chunk; pitch: a
+// staged row's size (cb rounded up to 16); mode: copy width 16 or 4 (cp.async)
+// or 2 (plain loads), chosen by the host from the alignment of rows and chunks.
+// Two stages: deeper rings measured no faster (the kernel is bound by its
+// instruction issue at small batches) and cost fp32 rows occupancy.
+template <int NT>
+constexpr int gv_stages() { return 2; }
+template <int T, int NT>
+__global__ void __launch_bounds__(kGvWarps * 32) gemv_staged_kernel(float *out, const unsigned char *w, int type,
+                                                                    int rows, int cols, const float *x, int nt,
+                                                                    size_t stride, int cb, int cb_tail, int pitch,
+                                                                    int mode) {
+    extern __shared__ __align__(16) unsigned char gsm[];
+    __shared__ float lut[16];
+    __shared__ __align__(16) float2 scales[kGvWarps * kGvRows * 8];  // Q4_K sub-block scales per warp and row
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int row0 = blockIdx.x * kGvRowsCta, first = blockIdx.y * NT;
+    const int n = min(NT, nt - first), nrows = min(kGvRowsCta, rows - row0);
+    const int stage_sz = kGvRowsCta * pitch + NT * kGvK * 4;
+    if (tid < 16) lut[tid] = static_cast<float>(kIq4nl[tid]);
+    auto stage = [&](int buf, int kc) {
+        unsigned char *ws = gsm + buf * stage_sz;
+        float *xs = reinterpret_cast<float *>(ws + kGvRowsCta * pitch);
+        const int kn = min(kGvK, cols - kc), bytes = kn == kGvK ? cb : cb_tail;
+        const size_t off = (size_t)(kc / kGvK) * cb;
+        // warp w copies rows w, w+8, ... and token vectors w, w+8, ...; lanes across the bytes
+        for (int r = warp; r < nrows; r += kGvWarps) {
+            unsigned char *d = ws + r * pitch;
+            const unsigned char *src = w + (size_t)(row0 + r) * stride + off;
+            if (mode == 16)
+                for (int o = lane * 16; o < bytes; o += 32 * 16) cp_async16(d + o, src + o);
+            else if (mode == 4)
+                for (int o = lane * 4; o < bytes; o += 32 * 4) cp_async4(d + o, src + o);
+            else
+                for (int o = lane * 2; o < bytes; o += 32 * 2)
+                    *reinterpret_cast<unsigned short *>(d + o) = __ldg(reinterpret_cast<const unsigned short *>(src + o));
+        }
+        for (int t = warp; t < n; t += kGvWarps) {
+            const float *src = x + (size_t)(first + t) * cols + kc;
+            for (int o = lane * 4; o < kn; o += 32 * 4) cp_async16(xs + t * kGvK + o, src + o);
+        }
+        cp_async_commit();
+    };
+    float acc[kGvRows][NT];
+#pragma unroll
+    for (int r = 0; r < kGvRows; r++)
+#pragma unroll
+        for (int t = 0; t < NT; t++) acc[r][t] = 0.0f;
+    const int r0 = warp * kGvRows, nr = min(kGvRows, nrows - r0);  // this warp's rows (nr <= 0: none)
+    constexpr int S = gv_stages<NT>();
+    const int nch = (cols + kGvK - 1) / kGvK;
+    // one copy group per chunk (empty past the end), so group c is chunk c's
+#pragma unroll
+    for (int c = 0; c < S - 1; c++) {
+        if (c < nch) stage(c, c * kGvK);
+        else cp_async_commit();
+    }
+    for (int c = 0; c < nch; c++) {
+        cp_async_wait<S - 2>();  // chunk c's copies have landed
+        __syncthreads();         // ... for every thread; and chunk c-1's buffer is free again
+        if (c + S - 1 < nch) stage((c + S - 1) % S, (c + S - 1) * kGvK);
+        else cp_async_commit();
+        const unsigned char *ws = gsm + (c % S) * stage_sz;
+        if (nr > 0)
+            gv_chunk<T, NT>(ws + r0 * pitch, pitch, nr, type,
+                            reinterpret_cast<const float *>(ws + kGvRowsCta * pitch), min(kGvK, cols - c * kGvK), n,
+                            lut, scales, acc);
+    }
+#pragma unroll
+    for (int r = 0; r < kGvRows; r++) {
+        if (r >= nr) break;
+#pragma unroll
+        for (int t = 0; t < NT; t++) {
+            if (t < n) {
+                const float s = lane_tree(acc[r][t]);
+                if (lane == 0) out[(size_t)(first + t) * rows + row0 + r0 + r] = s;
+            }
+        }
+    }
+}
+
 template <int TR, int TT>
 int launch_tiled(float *o, const float *w, int rows, int cols, const float *x, int nt, cudaStream_t st) {
     auto k = matmul_f32_tiled_kernel<TR, TT>;
     if (int rc = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, tiled_smem<TR, TT>())) return rc;
     k<<<dim3((rows + TR - 1) / TR, (nt + TT - 1) / TT), TR * TT / 2, tiled_smem<TR, TT>(), st>>>(o, w, rows, cols, x, nt);
     return cudaGetLastError();
+}
+
+template <int T, int NT>
+int launch_gv(float *o, const unsigned char *w, int type, int rows, int cols, const float *x, int nt, size_t stride,
+              int cb, int cbt, int pitch, int mode, cudaStream_t st) {
+    auto k = gemv_staged_kernel<T, NT>;
+    const int smem = gv_stages<NT>() * (kGvRowsCta * pitch + NT * kGvK * 4);
+    // the attribute is raised once per device, when a launch first needs more than the default
+    static int max_smem[64];
+    int dev = 0;
+    if (int rc = cudaGetDevice(&dev)) return rc;
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    if (smem > 48 * 1024 && smem > max_smem[dev]) {
+        if (int rc = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem)) return rc;
+        max_smem[dev] = smem;
+    }
+    k<<<dim3((rows + kGvRowsCta - 1) / kGvRowsCta, (nt + NT - 1) / NT), kGvWarps * 32, smem, st>>>(
+        o, w, type, rows, cols, x, nt, stride, cb, cbt, pitch, mode);
+    return cudaGetLastError();
+}
+
+template <int T>
+int launch_gv_nt(float *o, const unsigned char *w, int type, int rows, int cols, const float *x, int nt,
+                 size_t stride, int cb, int cbt, int pitch, int mode, cudaStream_t st) {
+    if (nt == 1) return launch_gv<T, 1>(o, w, type, rows, cols, x, nt, stride, cb, cbt, pitch, mode, st);
+    if (nt <= 4) return launch_gv<T, 4>(o, w, type, rows, cols, x, nt, stride, cb, cbt, pitch, mode, st);
+    return launch_gv<T, 16>(o, w, type, rows, cols, x, nt, stride, cb, cbt, pitch, mode, st);
 }
 
 __global__ void gather_kernel(float *out, const unsigned char *w, int type, int n, size_t stride, int row) {
@@ -186,8 +395,27 @@ int launch_matmul(float *o, const void *w, int type, int rows, int cols, const f
         if (rows >= 32) return launch_tiled<32, 32>(o, wf, rows, cols, x, nt, st);
         return launch_tiled<8, 16>(o, wf, rows, cols, x, nt, st);
     }
-    dim3 grid((rows + kRowsPerCta - 1) / kRowsPerCta, (nt + kTokTile - 1) / kTokTile);
     const unsigned char *wb = static_cast<const unsigned char *>(w);
+    if (cols % 32 == 0 && !(reinterpret_cast<uintptr_t>(x) & 15)) {
+        // staged kernel: chunks of kGvK columns (the last may be shorter), copied as wide as
+        // the rows' and chunks' alignment allows
+        const int cb = (int)row_bytes(type, kGvK), cbt = (int)row_bytes(type, cols % kGvK ? cols % kGvK : kGvK);
+        auto aligned = [&](int a) {
+            return reinterpret_cast<uintptr_t>(w) % a == 0 && stride % a == 0 && cb % a == 0 && cbt % a == 0;
+        };
+        const int mode = aligned(16) ? 16 : aligned(4) ? 4 : aligned(2) ? 2 : 0;
+        if (mode && cb > 0 && cbt > 0) {
+            const int pitch = (cb + 15) & ~15;
+            switch (type) {
+            case 0: return launch_gv_nt<0>(o, wb, type, rows, cols, x, nt, stride, cb, cbt, pitch, mode, st);
+            case 8: return launch_gv_nt<8>(o, wb, type, rows, cols, x, nt, stride, cb, cbt, pitch, mode, st);
+            case 12: return launch_gv_nt<12>(o, wb, type, rows, cols, x, nt, stride, cb, cbt, pitch, mode, st);
+            case 20: return launch_gv_nt<20>(o, wb, type, rows, cols, x, nt, stride, cb, cbt, pitch, mode, st);
+            default: return launch_gv_nt<-1>(o, wb, type, rows, cols, x, nt, stride, cb, cbt, pitch, mode, st);
+            }
+        }
+    }
+    dim3 grid((rows + kRowsPerCta - 1) / kRowsPerCta, (nt + kTokTile - 1) / kTokTile);
     switch (type) {
     case 0: matmul_kernel<0><<<grid, kRowsPerCta * 32, 0, st>>>(o, wb, type, rows, cols, x, nt, stride); break;
     case 12: matmul_kernel<12><<<grid, kRowsPerCta * 32, 0, st>>>(o, wb, type, rows, cols, x, nt, stride); break;

@@ -9,6 +9,7 @@ from __future__ import annotations
 
 import ctypes as C
 import os
+import threading
 from pathlib import Path
 
 import numpy as np
@@ -79,10 +80,27 @@ class CudaError(RuntimeError):
         self.code = code
 
 
+# Buffers released while this thread records a graph (qg_graph_begin .. qg_graph_end):
+# a cudaFree then would invalidate the capture, and Python may finalize a buffer at any
+# point (reference cycles are collected whenever the interpreter allocates), so their
+# frees wait until the capture ends.
+_capture = threading.local()
+
+
+def _deferring() -> list | None:
+    return getattr(_capture, "pending", None)
+
+
 def call(name: str, *args) -> None:
     """Call ``qg_<name>`` and raise on a non-zero cudaError_t."""
     lib = load()
     code = getattr(lib, "qg_" + name)(*args)
+    if name == "graph_begin" and not code:
+        _capture.pending = []
+    elif name == "graph_end":
+        pending, _capture.pending = _deferring() or [], None
+        for p in pending:
+            lib.qg_free(p)
     if code:
         raise CudaError(name, code, lib.qg_error(code).decode())
 
@@ -129,7 +147,11 @@ class Device:
 
     def free(self) -> None:
         if getattr(self, "p", None):
-            load().qg_free(self.p)
+            pending = _deferring()
+            if pending is not None:  # this thread is recording a graph
+                pending.append(self.p)
+            else:
+                load().qg_free(self.p)
             self.p = None
 
     def __del__(self):
