@@ -22,10 +22,12 @@ Keys beyond the contract: `parity` (layer 0 of this run against the CPU
 checker at N=1, against the single-GPU layer at N>1), `prefill` (config 4: one
 layer, T=2048, N(0,1) logits fed to top-10; with its CPU baseline and parity),
 `prefill_ep` (config 5's prefill: T=2048 through the router with the prefill
-ranking's bias and the shared expert; expert parallel at N>1), `configs`
-(config 1: T=4 Q4_K; config 2: T=17 IQ4_NL; the config-3 sweep T=1..17; the
-product shape 2560/640 with Q4_K gate/up and IQ4_NL down - each with its
-roofline and a CPU baseline), `roofline` (dominant kernel vs measured HBM copy
+ranking's bias and the shared expert; expert parallel at N>1, with whole-job
+tensor and HBM fractions), `configs` (config 1: T=4 Q4_K; config 2: T=17
+IQ4_NL; the config-3 sweep T=1..17; the product shape 2560/640 with Q4_K
+gate/up and IQ4_NL down at T=17 and its prefill at T=2048 - each with its
+roofline and a CPU baseline; the dense GEMV qg_matmul in five formats at T=1
+and 17, bitwise against qc_matmul), `roofline` (dominant kernel vs measured HBM copy
 bandwidth), `cpu_baseline` (the reference's own CPU MoE on this host's cores),
 `e2e` (the same metric through the C ABI with pinned host buffers copied in
 and results read back every step).
@@ -804,6 +806,13 @@ def main() -> None:
                                   (f"expert parallel over {world} GPUs (rank r returns its 1/{world} of the tokens)"
                                    if ep_mode else "one GPU"),
                       "tokens_per_s": P / (pms / 1e3), "ms_per_layer": pms}
+        # whole-job roofline over the N GPUs: the experts' tensor work (10 routed + the shared
+        # expert per token, 3 H x F products) and every weight byte read once plus x in, out written
+        ep_flops = P * (K + 1) * 3 * H * F * 2
+        ep_bytes = (E + 1) * EXPERT_BYTES + (E + 1) * H * 4 + 2 * P * H * 4
+        prefill_ep.update({"tflops": ep_flops / (pms / 1e3) / 1e12,
+                           "tensor_frac": ep_flops / (pms / 1e3) / 1e12 / (world * peaks["bf16_tflops"]),
+                           "hbm_frac": ep_bytes / (pms / 1e3) / 1e9 / (world * peaks["hbm_gbs"])})
         if ep_mode:
             # this rank's rows against the single-GPU layer
             sd = layer_seeds(0)
