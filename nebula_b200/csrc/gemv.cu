@@ -134,36 +134,46 @@ __global__ void __launch_bounds__(kTR * kTT / 2) matmul_f32_tiled_kernel(float *
 }
 
 // Staged GEMV for batches the tiled kernel does not take: a CTA of kGvWarps
-// warps owns kGvRows rows per warp. Each 256-column chunk of those rows and of
+// warps owns 2 rows per warp (4 for 8 or more tokens). Each 256-column chunk of those rows and of
 // the token vectors is copied into shared memory (two stages: the next chunk's
 // copies are in flight while one is multiplied), so a chunk's loads
 // are all issued at once instead of one dependent load per lane step. Lane j then
 // multiplies columns j, j+32, ... of the chunk in increasing order with one
 // fused multiply-add per element, continuing the same per-lane sums across
 // chunks: the order of matmul_kernel, so the results are bitwise the same.
-constexpr int kGvWarps = 8, kGvRows = 2, kGvK = 256;
-constexpr int kGvRowsCta = kGvWarps * kGvRows;
+constexpr int kGvWarps = 8, kGvK = 256;
 
 __device__ __forceinline__ void cp_async4(void *dst, const void *src) {
     asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src)
                  : "memory");
 }
 
-// Lane columns of one staged chunk of rows r0..r0+nr-1 (row r's bytes at
-// rows + r*pitch) against n token vectors xs[t][kGvK]: acc[r][t] += w * x in
-// increasing column order. T >= 0: that format; T < 0: `type`, per element.
-template <int T, int NT>
+// Rows per warp of the staged kernel for a token tile of NT.
+template <int NT>
+constexpr int gv_rows() { return NT >= 8 ? 4 : 2; }
+
+// Lane columns of one staged chunk of nr rows (row r's bytes at rows + r*pitch)
+// against n token vectors xs[t][kGvK], tokens in pairs: acc[r][p] holds tokens
+// 2p and 2p+1, each half a fused multiply-add with the rounding of a scalar one,
+// in increasing column order. T >= 0: that format; T < 0: `type`, per element.
+template <int T, int NT, int R>
 __device__ __forceinline__ void gv_chunk(const unsigned char *rows, int pitch, int nr, int type, const float *xs,
                                          int kn, int n, const float *lut, float2 *gv_scales,
-                                         float (&acc)[kGvRows][NT]) {
+                                         float2 (&acc)[R][(NT + 1) / 2]) {
+    constexpr int NP = (NT + 1) / 2;
     const int lane = threadIdx.x & 31;
+    auto load_x = [&](int k, float2 (&xv)[NP]) {
+#pragma unroll
+        for (int p = 0; p < NP; p++)
+            xv[p] = make_float2(2 * p < n ? xs[2 * p * kGvK + k] : 0.0f, 2 * p + 1 < n ? xs[(2 * p + 1) * kGvK + k] : 0.0f);
+    };
     if (T == 12) {  // one Q4_K superblock per chunk (kn = 256)
         // (d*sc, -dmin*m) of the 8 sub-blocks of each row, decoded by lanes 0..7 and
         // read back as broadcasts; nibbles become exact floats through the exponent
         // field (q + 2^23 - 2^23); w = d*sc*q - dmin*m with one rounding, in pairs
-        float2 *scl = gv_scales + (threadIdx.x >> 5) * (kGvRows * 8);
+        float2 *scl = gv_scales + (threadIdx.x >> 5) * (R * 8);
 #pragma unroll
-        for (int r = 0; r < kGvRows; r++) {
+        for (int r = 0; r < R; r++) {
             if (r < nr && lane < 8) {
                 const unsigned char *p = rows + r * pitch;
                 int s, m;
@@ -176,14 +186,11 @@ __device__ __forceinline__ void gv_chunk(const unsigned char *rows, int pitch, i
 #pragma unroll
         for (int i = 0; i < 4; i++) {
             const int k0 = 64 * i + lane;  // sub-block 2i; sub-block 2i+1 at k0 + 32
-            float x0[NT], x1[NT];
+            float2 x0[NP], x1[NP];
+            load_x(k0, x0);
+            load_x(k0 + 32, x1);
 #pragma unroll
-            for (int t = 0; t < NT; t++) {
-                x0[t] = t < n ? xs[t * kGvK + k0] : 0.0f;
-                x1[t] = t < n ? xs[t * kGvK + k0 + 32] : 0.0f;
-            }
-#pragma unroll
-            for (int r = 0; r < kGvRows; r++) {
+            for (int r = 0; r < R; r++) {
                 if (r < nr) {
                     const float4 sc = *reinterpret_cast<const float4 *>(scl + r * 8 + 2 * i);  // ds0, -dm0, ds1, -dm1
                     const unsigned b = rows[r * pitch + 16 + 32 * i + lane];
@@ -191,12 +198,11 @@ __device__ __forceinline__ void gv_chunk(const unsigned char *rows, int pitch, i
                                                             __uint_as_float((b >> 4) | 0x4B000000u)),
                                                 make_float2(-8388608.0f, -8388608.0f));
                     const float2 wv = __ffma2_rn(make_float2(sc.x, sc.z), q, make_float2(sc.y, sc.w));
+                    const float2 w0 = make_float2(wv.x, wv.x), w1 = make_float2(wv.y, wv.y);
 #pragma unroll
-                    for (int t = 0; t < NT; t++)
-                        if (t < n) acc[r][t] = __fmaf_rn(wv.x, x0[t], acc[r][t]);
+                    for (int p = 0; p < NP; p++) acc[r][p] = __ffma2_rn(w0, x0[p], acc[r][p]);
 #pragma unroll
-                    for (int t = 0; t < NT; t++)
-                        if (t < n) acc[r][t] = __fmaf_rn(wv.y, x1[t], acc[r][t]);
+                    for (int p = 0; p < NP; p++) acc[r][p] = __ffma2_rn(w1, x1[p], acc[r][p]);
                 }
             }
         }
@@ -205,11 +211,10 @@ __device__ __forceinline__ void gv_chunk(const unsigned char *rows, int pitch, i
     }
     for (int m = 0; m < kn / 32; m++) {
         const int k = 32 * m + lane;
-        float xv[NT];
+        float2 xv[NP];
+        load_x(k, xv);
 #pragma unroll
-        for (int t = 0; t < NT; t++) xv[t] = t < n ? xs[t * kGvK + k] : 0.0f;
-#pragma unroll
-        for (int r = 0; r < kGvRows; r++) {
+        for (int r = 0; r < R; r++) {
             if (r >= nr) break;
             const unsigned char *p = rows + r * pitch;
             float a;
@@ -225,9 +230,9 @@ __device__ __forceinline__ void gv_chunk(const unsigned char *rows, int pitch, i
             } else {
                 a = decode_at(p, T < 0 ? type : T, k);
             }
+            const float2 a2 = make_float2(a, a);
 #pragma unroll
-            for (int t = 0; t < NT; t++)
-                if (t < n) acc[r][t] = __fmaf_rn(a, xv[t], acc[r][t]);
+            for (int p2 = 0; p2 < NP; p2++) acc[r][p2] = __ffma2_rn(a2, xv[p2], acc[r][p2]);
         }
     }
 }
@@ -246,15 +251,16 @@ __global__ void __launch_bounds__(kGvWarps * 32) gemv_staged_kernel(float *out, 
                                                                     int mode) {
     extern __shared__ __align__(16) unsigned char gsm[];
     __shared__ float lut[16];
-    __shared__ __align__(16) float2 scales[kGvWarps * kGvRows * 8];  // Q4_K sub-block scales per warp and row
+    constexpr int R = gv_rows<NT>(), kRowsCta = kGvWarps * R, NP = (NT + 1) / 2;
+    __shared__ __align__(16) float2 scales[kGvWarps * R * 8];  // Q4_K sub-block scales per warp and row
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int row0 = blockIdx.x * kGvRowsCta, first = blockIdx.y * NT;
-    const int n = min(NT, nt - first), nrows = min(kGvRowsCta, rows - row0);
-    const int stage_sz = kGvRowsCta * pitch + NT * kGvK * 4;
+    const int row0 = blockIdx.x * kRowsCta, first = blockIdx.y * NT;
+    const int n = min(NT, nt - first), nrows = min(kRowsCta, rows - row0);
+    const int stage_sz = kRowsCta * pitch + NT * kGvK * 4;
     if (tid < 16) lut[tid] = static_cast<float>(kIq4nl[tid]);
     auto stage = [&](int buf, int kc) {
         unsigned char *ws = gsm + buf * stage_sz;
-        float *xs = reinterpret_cast<float *>(ws + kGvRowsCta * pitch);
+        float *xs = reinterpret_cast<float *>(ws + kRowsCta * pitch);
         const int kn = min(kGvK, cols - kc), bytes = kn == kGvK ? cb : cb_tail;
         const size_t off = (size_t)(kc / kGvK) * cb;
         // warp w copies rows w, w+8, ... and token vectors w, w+8, ...; lanes across the bytes
@@ -275,12 +281,12 @@ __global__ void __launch_bounds__(kGvWarps * 32) gemv_staged_kernel(float *out, 
         }
         cp_async_commit();
     };
-    float acc[kGvRows][NT];
+    float2 acc[R][NP];
 #pragma unroll
-    for (int r = 0; r < kGvRows; r++)
+    for (int r = 0; r < R; r++)
 #pragma unroll
-        for (int t = 0; t < NT; t++) acc[r][t] = 0.0f;
-    const int r0 = warp * kGvRows, nr = min(kGvRows, nrows - r0);  // this warp's rows (nr <= 0: none)
+        for (int p = 0; p < NP; p++) acc[r][p] = make_float2(0.0f, 0.0f);
+    const int r0 = warp * R, nr = min(R, nrows - r0);  // this warp's rows (nr <= 0: none)
     constexpr int S = gv_stages<NT>();
     const int nch = (cols + kGvK - 1) / kGvK;
     // one copy group per chunk (empty past the end), so group c is chunk c's
@@ -296,17 +302,17 @@ __global__ void __launch_bounds__(kGvWarps * 32) gemv_staged_kernel(float *out, 
         else cp_async_commit();
         const unsigned char *ws = gsm + (c % S) * stage_sz;
         if (nr > 0)
-            gv_chunk<T, NT>(ws + r0 * pitch, pitch, nr, type,
-                            reinterpret_cast<const float *>(ws + kGvRowsCta * pitch), min(kGvK, cols - c * kGvK), n,
+            gv_chunk<T, NT, R>(ws + r0 * pitch, pitch, nr, type,
+                               reinterpret_cast<const float *>(ws + kRowsCta * pitch), min(kGvK, cols - c * kGvK), n,
                             lut, scales, acc);
     }
 #pragma unroll
-    for (int r = 0; r < kGvRows; r++) {
+    for (int r = 0; r < R; r++) {
         if (r >= nr) break;
 #pragma unroll
         for (int t = 0; t < NT; t++) {
             if (t < n) {
-                const float s = lane_tree(acc[r][t]);
+                const float s = lane_tree((t & 1) ? acc[r][t >> 1].y : acc[r][t >> 1].x);
                 if (lane == 0) out[(size_t)(first + t) * rows + row0 + r0 + r] = s;
             }
         }
@@ -325,7 +331,8 @@ template <int T, int NT>
 int launch_gv(float *o, const unsigned char *w, int type, int rows, int cols, const float *x, int nt, size_t stride,
               int cb, int cbt, int pitch, int mode, cudaStream_t st) {
     auto k = gemv_staged_kernel<T, NT>;
-    const int smem = gv_stages<NT>() * (kGvRowsCta * pitch + NT * kGvK * 4);
+    constexpr int kRowsCta = kGvWarps * gv_rows<NT>();
+    const int smem = gv_stages<NT>() * (kRowsCta * pitch + NT * kGvK * 4);
     // the attribute is raised once per device, when a launch first needs more than the default
     static int max_smem[64];
     int dev = 0;
@@ -335,7 +342,7 @@ int launch_gv(float *o, const unsigned char *w, int type, int rows, int cols, co
         if (int rc = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem)) return rc;
         max_smem[dev] = smem;
     }
-    k<<<dim3((rows + kGvRowsCta - 1) / kGvRowsCta, (nt + NT - 1) / NT), kGvWarps * 32, smem, st>>>(
+    k<<<dim3((rows + kRowsCta - 1) / kRowsCta, (nt + NT - 1) / NT), kGvWarps * 32, smem, st>>>(
         o, w, type, rows, cols, x, nt, stride, cb, cbt, pitch, mode);
     return cudaGetLastError();
 }
@@ -345,6 +352,8 @@ int launch_gv_nt(float *o, const unsigned char *w, int type, int rows, int cols,
                  size_t stride, int cb, int cbt, int pitch, int mode, cudaStream_t st) {
     if (nt == 1) return launch_gv<T, 1>(o, w, type, rows, cols, x, nt, stride, cb, cbt, pitch, mode, st);
     if (nt <= 4) return launch_gv<T, 4>(o, w, type, rows, cols, x, nt, stride, cb, cbt, pitch, mode, st);
+    if (nt <= 8) return launch_gv<T, 8>(o, w, type, rows, cols, x, nt, stride, cb, cbt, pitch, mode, st);
+    if (nt == 17 || nt == 18) return launch_gv<T, 18>(o, w, type, rows, cols, x, nt, stride, cb, cbt, pitch, mode, st);
     return launch_gv<T, 16>(o, w, type, rows, cols, x, nt, stride, cb, cbt, pitch, mode, st);
 }
 
