@@ -641,6 +641,8 @@ def main() -> None:
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--no-configs", action="store_true", help="skip configs 1, 2, the T sweep and the product shape")
+    ap.add_argument("--dense-only", action="store_true",
+                    help="print only the dense GEMV measurement (qg_matmul, five formats) as one JSON line")
     ap.add_argument("--routes", default=None,
                     help="also replay this QROUTE1 route trace (the reference's route profiler output) through "
                          "qg_moe_routed on the stack's layers (record layer modulo the stack depth)")
@@ -669,6 +671,10 @@ def main() -> None:
     T = args.tokens
     ep_mode = world > 1
     peaks = measured_peaks()
+    if args.dense_only:
+        if rank == 0:
+            print(json.dumps({"dense_gemv": dense_gemv(torch, L, peaks, not args.no_cpu, args.steps)}))
+        return
     stack = Stack(L, args.layers, T, seed0=0, ep=(rank, world) if ep_mode else None)
     L.call("sync")
     graph = stack.capture()
