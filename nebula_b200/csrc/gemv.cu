@@ -187,8 +187,13 @@ __device__ __forceinline__ void gv_chunk(const unsigned char *rows, int pitch, i
         for (int i = 0; i < 4; i++) {
             const int k0 = 64 * i + lane;  // sub-block 2i; sub-block 2i+1 at k0 + 32
             float2 x0[NP], x1[NP];
-            load_x(k0, x0);
-            load_x(k0 + 32, x1);
+            if constexpr (NT == 1) {  // one token: scalar multiply-adds on .x
+                x0[0].x = xs[k0];
+                x1[0].x = xs[k0 + 32];
+            } else {
+                load_x(k0, x0);
+                load_x(k0 + 32, x1);
+            }
 #pragma unroll
             for (int r = 0; r < R; r++) {
                 if (r < nr) {
@@ -198,21 +203,28 @@ __device__ __forceinline__ void gv_chunk(const unsigned char *rows, int pitch, i
                                                             __uint_as_float((b >> 4) | 0x4B000000u)),
                                                 make_float2(-8388608.0f, -8388608.0f));
                     const float2 wv = __ffma2_rn(make_float2(sc.x, sc.z), q, make_float2(sc.y, sc.w));
-                    const float2 w0 = make_float2(wv.x, wv.x), w1 = make_float2(wv.y, wv.y);
+                    if constexpr (NT == 1) {
+                        acc[r][0].x = __fmaf_rn(wv.x, x0[0].x, acc[r][0].x);
+                        acc[r][0].x = __fmaf_rn(wv.y, x1[0].x, acc[r][0].x);
+                    } else {
+                        const float2 w0 = make_float2(wv.x, wv.x), w1 = make_float2(wv.y, wv.y);
 #pragma unroll
-                    for (int p = 0; p < NP; p++) acc[r][p] = __ffma2_rn(w0, x0[p], acc[r][p]);
+                        for (int p = 0; p < NP; p++) acc[r][p] = __ffma2_rn(w0, x0[p], acc[r][p]);
 #pragma unroll
-                    for (int p = 0; p < NP; p++) acc[r][p] = __ffma2_rn(w1, x1[p], acc[r][p]);
+                        for (int p = 0; p < NP; p++) acc[r][p] = __ffma2_rn(w1, x1[p], acc[r][p]);
+                    }
                 }
             }
         }
         __syncwarp();  // the scales are rewritten for the next chunk
         return;
     }
+#pragma unroll(NT == 1 ? 8 : 1)
     for (int m = 0; m < kn / 32; m++) {
         const int k = 32 * m + lane;
         float2 xv[NP];
-        load_x(k, xv);
+        if constexpr (NT == 1) xv[0].x = xs[k];  // one token: scalar multiply-adds on .x
+        else load_x(k, xv);
 #pragma unroll
         for (int r = 0; r < R; r++) {
             if (r >= nr) break;
@@ -230,9 +242,13 @@ __device__ __forceinline__ void gv_chunk(const unsigned char *rows, int pitch, i
             } else {
                 a = decode_at(p, T < 0 ? type : T, k);
             }
-            const float2 a2 = make_float2(a, a);
+            if constexpr (NT == 1) {
+                acc[r][0].x = __fmaf_rn(a, xv[0].x, acc[r][0].x);
+            } else {
+                const float2 a2 = make_float2(a, a);
 #pragma unroll
-            for (int p2 = 0; p2 < NP; p2++) acc[r][p2] = __ffma2_rn(a2, xv[p2], acc[r][p2]);
+                for (int p2 = 0; p2 < NP; p2++) acc[r][p2] = __ffma2_rn(a2, xv[p2], acc[r][p2]);
+            }
         }
     }
 }
