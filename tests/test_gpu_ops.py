@@ -55,7 +55,7 @@ def test_matmul_bitwise_vs_qc_matmul(L, ref2048, typ):
         rows = 13
         w = random_blocks(rng, typ, rows, cols, d=0.002, dmin=0.001)
         dw = L.Device(w)
-        for nt in (1, 4, 16, 17, 33, 512, 2048):
+        for nt in (1, 2, 4, 5, 8, 9, 16, 17, 18, 19, 33, 512, 2048):
             x = (rng.normal(size=(nt, cols)) * 0.2).astype(np.float32)
             dx = L.Device(x)
             out = L.Device.empty((nt, rows), np.float32)
@@ -252,6 +252,37 @@ def test_graph_replay_equals_eager(L, ref2048):
             L.call("graph_launch", g)
             np.testing.assert_array_equal(out.get(), ref2048.matmul(w, 12, 64, 2048, x))
     finally:
+        L.load().qg_graph_destroy(g)
+
+
+def test_buffer_collected_during_capture_is_freed_after_it(L, ref2048):
+    """A device buffer that Python finalizes while this thread records a graph (a
+    reference cycle collected mid-capture) is freed at qg_graph_end, not during the
+    capture, whose cudaFree would invalidate it."""
+    import gc
+
+    class Cycle:
+        pass
+
+    rng = np.random.default_rng(3)
+    w = random_blocks(rng, 12, 32, 512)
+    x = rng.normal(size=(3, 512)).astype(np.float32)
+    dw, dx = L.Device(w), L.Device(x)
+    out = L.Device(np.zeros((3, 32), np.float32))
+    c = Cycle()
+    c.me, c.buf = c, L.Device(nbytes=1 << 20)
+    del c
+    g = C.c_void_p()
+    gc.disable()
+    L.call("graph_begin", C.byref(g))
+    try:
+        gc.collect()  # finalizes the cycle's buffer inside the capture
+        L.call("matmul", out.p, dw.p, 12, 32, 512, dx.p, 3)
+        L.call("graph_end", g)
+        L.call("graph_launch", g)
+        np.testing.assert_array_equal(out.get(), ref2048.matmul(w, 12, 32, 512, x))
+    finally:
+        gc.enable()
         L.load().qg_graph_destroy(g)
 
 
