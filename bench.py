@@ -241,8 +241,27 @@ def layer_seeds(l: int, seed0: int = 0) -> dict:
             "sr": s + 8, "x": 2 + l + 7919 * seed0}
 
 
+class View:
+    """A slice of a larger device buffer (it owns nothing): `p`, `nbytes` and `get()`."""
+
+    def __init__(self, L, base, offset: int, shape, dtype):
+        self.L, self.base = L, base
+        self.p = base.p + offset
+        self.shape, self.dtype = tuple(shape), np.dtype(dtype)
+        self.nbytes = int(np.prod(self.shape)) * self.dtype.itemsize
+
+    def get(self) -> np.ndarray:
+        out = np.empty(self.shape, self.dtype)
+        self.L.call("read", out.ctypes.data, self.p, out.nbytes)
+        return out
+
+
 class Stack:
     """Resident layers on the device plus per-layer inputs and outputs.
+
+    The layers' inputs are slices of one buffer (`xall`, [layers][T][h]) and so are
+    their outputs (`oall`), so a whole step's activations cross the host link in one
+    copy each way.
 
     With ``ep=(rank, world)`` the rank keeps only its share of each layer's
     experts (snake order of the layer's ranking) and runs the expert-parallel
@@ -253,6 +272,8 @@ class Stack:
         self.L, self.T, self.layers, self.ep = L, T, layers, ep
         self.h, self.f, self.gt, self.dt, self.seed0 = h, f, gt, dt, seed0
         self.w = []
+        act = T * h * 4
+        self.xall, self.oall = L.Device(nbytes=layers * act), L.Device(nbytes=layers * act)
         if ep:
             from nebula_b200 import ep as epm
             rank, world = ep
@@ -275,10 +296,11 @@ class Stack:
             if shared:
                 d.update({"sg": L.synth_weights(gt, f, h, sd["sg"]), "su": L.synth_weights(gt, f, h, sd["su"]),
                           "sd": L.synth_weights(dt, h, f, sd["sd"]), "sr": L.synth_weights(0, 1, h, sd["sr"])})
+            L.call("synth_normal", C.c_void_p(self.xall.p + l * act), T * h, sd["x"], C.c_float(1.0))
             d.update({
                 "bias": L.Device(zipf_bias(l)) if bias else None,
-                "x": L.synth_normal(T * h, sd["x"]),
-                "out": L.Device.empty((T, h), np.float32),
+                "x": View(L, self.xall, l * act, (T * h,), np.float32),
+                "out": View(L, self.oall, l * act, (T, h), np.float32),
                 "ids": L.Device.empty((T, K), np.int32), "wts": L.Device.empty((T, K), np.float32),
             })
             self.w.append(d)
@@ -740,12 +762,10 @@ def main() -> None:
     hout = torch.empty((args.layers, T, H), dtype=torch.float32, pin_memory=True)
     nbytes = T * H * 4
 
-    def e2e_step():
-        for l in range(args.layers):
-            L.call("write", stack.w[l]["x"].p, hx[l].data_ptr(), nbytes)
+    def e2e_step():  # the 48 layers' inputs and outputs are contiguous: one copy each way
+        L.call("write", stack.xall.p, hx.data_ptr(), args.layers * nbytes)
         L.call("graph_launch", graph)
-        for l in range(args.layers):
-            L.call("read", hout[l].data_ptr(), stack.w[l]["out"].p, nbytes)
+        L.call("read", hout.data_ptr(), stack.oall.p, args.layers * nbytes)
 
     e2e_step()
     barrier()
