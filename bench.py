@@ -487,7 +487,7 @@ def event_ms(torch, fn, reps: int) -> float:
 
 
 def read_profile(L) -> dict:
-    phases = ("router", "route", "plan", "gate_up", "down", "combine", "experts", "decode_router")
+    phases = ("router", "route", "plan", "gate_up", "down", "combine", "experts", "decode_router", "lean")
     prof = {}
     for i, name in enumerate(phases):
         tot, n = C.c_double(0), C.c_int(0)
@@ -520,6 +520,8 @@ def single_layer_config(torch, L, peaks, T: int, h: int, f: int, gt: int, dt: in
     kbytes = (float(np.mean(used)) + (1 if shared else 0)) * eb + 2 * T * h * 4
     if kern == "decode_router":
         kbytes = (E + 1) * h * 4 + T * h * 4 + T * K * 8
+    elif kern == "lean":  # the whole layer in one kernel: the router's rows too
+        kbytes += (E + 1) * h * 4
     res = {"workload": what, "tokens": T, "tokens_per_s": T / (ms_layer / 1e3), "ms_per_layer": ms_layer,
            "experts_used_mean": float(np.mean(used)), "layer_bytes": lb,
            "hbm_gbs": lb / (ms_layer / 1e3) / 1e9, "hbm_frac": lb / (ms_layer / 1e3) / 1e9 / peaks["hbm_gbs"],

@@ -46,7 +46,8 @@ namespace {
 // Only eager launches on the legacy stream are timed; graph captures are not.
 // kExpertsFused: one kernel doing gate/up, SwiGLU, down and the combine;
 // kDecodeRouter: one kernel doing the router GEMV, top-10 and the plan.
-enum Phase { kRouter, kRoute, kPlan, kGateUp, kDown, kCombine, kExpertsFused, kDecodeRouter, kPhases };
+// kLean: the whole layer in one kernel (batches of 1 or 2 tokens).
+enum Phase { kRouter, kRoute, kPlan, kGateUp, kDown, kCombine, kExpertsFused, kDecodeRouter, kLean, kPhases };
 struct Profiler {
     bool on = false;
     std::vector<cudaEvent_t> pool;
@@ -1263,6 +1264,10 @@ extern "C" int qg_moe_layer(float *out, int *ids_out, float *weights_out, const 
         a.sg = static_cast<const unsigned char *>(sg);
         a.su = static_cast<const unsigned char *>(su);
         a.sd = static_cast<const unsigned char *>(sd);
+        if (lean_supported(a)) {
+            Span sp(kLean, st);
+            return lean_run(a, st);
+        }
         return dec_run_timed(a, st);
     }
     Layout L = layout(tokens, hidden, ffn);

@@ -1,6 +1,7 @@
 // Interface between the MoE entry points (moe.cu) and the decode kernels
 // (moe_decode.cu), and the fixed workspace prefix both paths share.
 #pragma once
+#include <cstddef>
 #include "common.cuh"
 #include "moe_tc.cuh"
 
@@ -15,11 +16,13 @@ struct DecHdr {
     int invalid_tokens, n_pairs, n_used, error;
 };
 struct DecCtr {
-    int k1_ticket, queue, k2_ticket, tc_queue, tc_ticket, k1_routed, pad[10];
+    int k1_ticket, queue, k2_ticket, tc_queue, tc_ticket, k1_routed, pad[8];
+    unsigned long long lean_barrier;  // the lean kernel's grid barrier: arrivals, only growing
     int gu_done[kExperts + 1];
     int tilecnt[kMaxDecodeTokens * 64];
     int gu_pcnt[(kExperts + 1) * kMaxGuTiles];  // K parts finished per gate/up tile
 };
+static_assert(offsetof(DecCtr, lean_barrier) % 8 == 0, "64-bit barrier counter");
 constexpr size_t kHdrBytes = 256;
 constexpr size_t kPrefixBytes = (kHdrBytes + sizeof(DecCtr) + 255) & ~size_t(255);
 
@@ -69,5 +72,9 @@ bool dec_supported(int T, int H, int F, int QG, int QD);
 // split != null (profiling): recorded between the router/plan kernel and the
 // expert kernel, which is then launched without programmatic overlap.
 int dec_run(const DecArgs &a, cudaStream_t st, cudaEvent_t split = nullptr);
+// The lean single-kernel layer (moe_lean.cu): 1 or 2 tokens, hidden 2048 / ffn
+// 512, Q4_K experts, router given, one GPU.
+bool lean_supported(const DecArgs &a);
+int lean_run(const DecArgs &a, cudaStream_t st);
 
 }  // namespace nb

@@ -1,0 +1,354 @@
+// Lean decode layer for batches of 1 or 2 tokens: the whole routed-MoE layer
+// (router GEMV, top-10, gate/up + SwiGLU, down x route weight, combine and the
+// gated shared expert) in ONE cooperative kernel of one CTA per SM.
+//
+// At these batch sizes the tensor cores have nothing to multiply (N = T), and
+// the general decode path's time is its chain of hand-offs: the router kernel,
+// the plan, the work queue, per-chunk role hand-offs and per-tile tails. Here
+// every warp streams weight rows with all of a row's loads issued at once, and
+// the phases are separated by two grid-wide barriers:
+//   1. the router GEMV (512 rows + the shared-gate row), one warp per row, in the
+//      reference's 32-lane order, so the logits and expert ids are bit-exact;
+//   2. every CTA computes the top-10 of each token itself (identical results),
+//      and gate/up + SwiGLU rows are dealt to all warps: (token, slot, row) of
+//      each routed pair and of the shared expert -> mid;
+//   3. each warp takes output rows: for one token and one row it reads the ten
+//      routed experts' down rows and the shared expert's down row, and sums
+//      w_k * (down_k . mid_k) plus sigmoid(gate) * (shared . mid) - the combine
+//      happens in the same pass, with no slot rows.
+// Each weight row is copied into the warp's shared memory with 16-byte loads
+// (all of a row's loads in flight at once), then lane j multiplies byte j of
+// every 32-byte block of quantized values, so the activations the lanes read
+// are consecutive (no bank conflicts). Expert outputs match the reference within
+// the float tolerance of the path (each weight is d*sc*q - dmin*m with one
+// rounding, summed in another order than the reference's); routing is bitwise
+// the reference's.
+//
+// The barriers are waits on other CTAs, so the kernel is launched cooperatively
+// (every CTA resident) and each wait gives up after a bound, raising the error
+// word instead of hanging; after such an error the workspace must be zeroed
+// again (as after any error), which also restarts the barrier counter.
+#include "moe_decode.cuh"
+#include "quant.cuh"
+#include "route.cuh"
+
+using namespace nb;
+
+namespace {
+
+constexpr int kLeanH = 2048, kLeanF = 512;    // the shape this kernel is built for
+constexpr int kLeanThreads = 512, kLeanWarps = kLeanThreads / 32;
+constexpr int kLeanMaxT = 4;
+constexpr int kSbH = kLeanH / 256, kSbF = kLeanF / 256;  // Q4_K superblocks per gate/up row, per down row
+constexpr int kChH = kSbH * 9, kChF = kSbF * 9;          // 16-byte chunks per row
+constexpr int kMaxSb = 2 * kSbH > 11 * kSbF ? 2 * kSbH : 11 * kSbF;  // superblocks of one warp item
+// gate/up: the two rows' chunks over 32 lanes; down: eleven rows' chunks
+constexpr int kGuPer = (2 * kChH + 31) / 32, kDnPer = (11 * kChF + 31) / 32;
+
+__device__ __forceinline__ int ld_acquire_gpu(const int *p) {
+    int v;
+    asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Grid-wide barrier over the resident CTAs (cooperative launch) on one 64-bit
+// counter that only grows: every CTA adds 1 per barrier with a non-returning
+// release add (no serialised returning atomics), and barrier k of a launch is
+// passed once the counter reaches base + k * grid. A launch makes exactly two
+// barriers, so base = the counter rounded down to a multiple of 2 * grid when the
+// CTA starts (the counter then holds at most grid - 1 arrivals of this launch).
+// Bounded: false (and error bit 4) after kWaitLimitNs.
+__device__ __forceinline__ unsigned long long ld_acquire_u64(const unsigned long long *p) {
+    unsigned long long v;
+    asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ bool grid_barrier(unsigned long long *ctr, unsigned long long target, int *err, volatile int *s_ok) {
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        asm volatile("red.release.gpu.global.add.u64 [%0], 1;" ::"l"(ctr) : "memory");
+        if (ld_acquire_u64(ctr) < target) {
+            const uint64_t t0 = global_ns();
+            while (ld_acquire_u64(ctr) < target) {
+                if (global_ns() - t0 > kWaitLimitNs) {
+                    atomicOr(err, 4);
+                    *s_ok = 0;
+                    break;
+                }
+            }
+        }
+    }
+    __syncthreads();
+    return *s_ok != 0;
+}
+
+// (d*sc, dmin*m) of every sub-block of nh superblocks whose rows sit in the
+// warp's buffer (row r of `rb` bytes, sbs superblocks each), one (superblock,
+// sub-block) per lane and step: scl[h*8 + g] for superblock h = r*sbs + sb.
+__device__ __forceinline__ void q4k_scales(const unsigned char *buf, int rb, int sbs, int nh, float2 *scl) {
+    for (int pg = threadIdx.x & 31; pg < nh * 8; pg += 32) {
+        const int h = pg >> 3, g = pg & 7;
+        const unsigned char *hd = buf + (h / sbs) * rb + (h % sbs) * 144;
+        int sc, m;
+        k_scale_min(hd + 4, g, sc, m);
+        scl[pg] = make_float2(half_at(hd) * static_cast<float>(sc), half_at(hd + 2) * static_cast<float>(m));
+    }
+}
+
+// Two Q4_K values of byte b (low nibble: sub-block 2i, high: 2i+1) as exact floats.
+__device__ __forceinline__ float2 nibbles(unsigned b) {
+    return __fadd2_rn(make_float2(__uint_as_float((b & 15u) | 0x4B000000u), __uint_as_float((b >> 4) | 0x4B000000u)),
+                      make_float2(-8388608.0f, -8388608.0f));
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int d = 16; d; d >>= 1) v += __shfl_xor_sync(0xffffffffu, v, d);
+    return v;
+}
+
+}  // namespace
+
+namespace {
+
+// Shared memory: activations (x [T][H] in phases 1-2, then mid [P][F] in phase 3),
+// and per warp the (d*sc, dmin*m) of the superblocks of its current item.
+constexpr int kActFloats = (kLeanMaxT * kLeanH > (kLeanMaxT * kTop + kLeanMaxT) * kLeanF)
+                               ? kLeanMaxT * kLeanH
+                               : (kLeanMaxT * kTop + kLeanMaxT) * kLeanF;
+// per warp: its item's weight rows (two gate/up rows or eleven down rows, 16-byte chunks)
+constexpr int kWBuf = ((2 * kChH > 11 * kChF ? 2 * kChH : 11 * kChF) * 16 + 127) / 128 * 128;
+constexpr int kLeanSmem = kActFloats * 4 + kLeanWarps * kMaxSb * 8 * 8 + kLeanWarps * kWBuf;
+
+__global__ void __launch_bounds__(kLeanThreads, 1) lean_moe_kernel(DecArgs a) {
+    extern __shared__ __align__(16) float lsm[];
+    float *act = lsm;
+    float2 *wscl = reinterpret_cast<float2 *>(lsm + kActFloats) + (threadIdx.x >> 5) * (kMaxSb * 8);
+    unsigned char *wbuf = reinterpret_cast<unsigned char *>(lsm + kActFloats) + kLeanWarps * kMaxSb * 8 * 8 +
+                          (threadIdx.x >> 5) * kWBuf;
+    __shared__ int s_ids[kLeanMaxT * kTop];
+    __shared__ float s_w[kLeanMaxT * kTop], s_sig[kLeanMaxT];
+    __shared__ int s_ok;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int T = a.T, gw = blockIdx.x * kLeanWarps + warp, nw = gridDim.x * kLeanWarps;
+    const bool shared = a.sg != nullptr;
+    unsigned long long *ctr = &a.ctr->lean_barrier;
+    int *err = &a.hdr->error;
+    __shared__ unsigned long long s_base;
+    if (tid == 0) {
+        s_ok = 1;
+        const unsigned long long c0 = ld_acquire_u64(ctr), round = 2ull * gridDim.x;
+        s_base = c0 - c0 % round;
+    }
+    for (int i = tid; i < T * kLeanH / 4; i += kLeanThreads)
+        reinterpret_cast<float4 *>(act)[i] = __ldg(reinterpret_cast<const float4 *>(a.x) + i);
+    __syncthreads();
+
+    // 1. router GEMV (and the shared-gate row): lane j adds k = j, j+32, ... in order
+    const int rrows = kExperts + (a.s_router ? 1 : 0);
+    for (int row = gw; row < rrows; row += nw) {
+        const float *w = row < kExperts ? a.router + (size_t)row * kLeanH : a.s_router;
+        float acc[kLeanMaxT];
+#pragma unroll
+        for (int t = 0; t < kLeanMaxT; t++) acc[t] = 0.0f;
+#pragma unroll
+        for (int h = 0; h < kLeanH / 1024; h++) {
+            float wv[32];  // a row's loads are all in flight before the first multiply-add
+#pragma unroll
+            for (int i = 0; i < 32; i++) wv[i] = __ldg(w + h * 1024 + 32 * i + lane);
+#pragma unroll
+            for (int i = 0; i < 32; i++) {
+                const int k = h * 1024 + 32 * i + lane;
+#pragma unroll
+                for (int t = 0; t < kLeanMaxT; t++)
+                    if (t < T) acc[t] = __fmaf_rn(wv[i], act[t * kLeanH + k], acc[t]);
+            }
+        }
+#pragma unroll
+        for (int t = 0; t < kLeanMaxT; t++) {
+            if (t < T) {
+                const float s = lane_tree(acc[t]);
+                if (lane == 0) {
+                    if (row < kExperts) a.logits[t * kExperts + row] = s;
+                    else a.sgate[t] = s;
+                }
+            }
+        }
+    }
+    if (!grid_barrier(ctr, s_base + gridDim.x, err, &s_ok)) return;
+
+    // 2. top-10 of every token, in every CTA
+    if (warp < T) route_token_warp(a.logits + warp * kExperts, a.bias, s_ids + warp * kTop, s_w + warp * kTop);
+    if (tid < T && shared) s_sig[tid] = sigmoidf_ref(__ldcg(a.sgate + tid));
+    __syncthreads();
+    if (blockIdx.x == 0) {
+        if (tid < T * kTop) {
+            a.ids[tid] = s_ids[tid];
+            a.wts[tid] = s_w[tid];
+        }
+        if (tid == 0) {  // status words: pairs computed, distinct experts, tokens with NaN rows
+            int pairs = 0, used = 0, bad = 0;
+            for (int t = 0; t < T; t++) {
+                if (s_ids[t * kTop] < 0) bad++;
+                else pairs += kTop;
+            }
+            for (int i = 0; i < T * kTop; i++) {
+                const int e = s_ids[i];
+                bool first = e >= 0;
+                for (int j = 0; j < i && first; j++) first = s_ids[j] != e;
+                used += first;
+            }
+            a.hdr->n_pairs = pairs;
+            a.hdr->n_used = used;
+            a.hdr->invalid_tokens = bad;
+        }
+    }
+    //    gate/up + SwiGLU: item = (pair p, row); pairs 0..10T-1 routed, 10T.. the shared expert's
+    const int P = T * kTop + (shared ? T : 0);
+    for (int it = gw; it < P * kLeanF; it += nw) {
+        const int p = it / kLeanF, row = it % kLeanF;
+        int t;
+        const unsigned char *g, *u;
+        if (p < T * kTop) {
+            t = p / kTop;
+            const int e = s_ids[p];
+            if (e < 0) continue;  // a token whose logits were not finite: no contributions
+            g = a.gate + ((size_t)e * kLeanF + row) * a.grb;
+            u = a.up + ((size_t)e * kLeanF + row) * a.grb;
+        } else {
+            t = p - T * kTop;
+            g = a.sg + (size_t)row * a.grb;
+            u = a.su + (size_t)row * a.grb;
+        }
+        uint4 v[kGuPer];
+#pragma unroll
+        for (int i = 0; i < kGuPer; i++) {
+            const int f = lane + 32 * i;
+            if (f < 2 * kChH) {
+                v[i] = __ldg(reinterpret_cast<const uint4 *>(f < kChH ? g : u) + (f < kChH ? f : f - kChH));
+                reinterpret_cast<uint4 *>(wbuf)[f] = v[i];  // gate row at byte 0, up row at kChH*16
+            }
+        }
+        __syncwarp();
+        q4k_scales(wbuf, kChH * 16, kSbH, 2 * kSbH, wscl);
+        __syncwarp();
+        // lane j takes byte j of every 32-byte q block: its activations are consecutive
+        // across lanes, and each is loaded once for the gate and the up row
+        const float *xt = act + t * kLeanH;
+        float2 ag = make_float2(0.0f, 0.0f), au = make_float2(0.0f, 0.0f);
+#pragma unroll 2
+        for (int sb = 0; sb < kSbH; sb++) {
+            const unsigned char *qg = wbuf + sb * 144 + 16, *qu = qg + kChH * 16;
+            const float4 *sg = reinterpret_cast<const float4 *>(wscl + sb * 8);
+            const float4 *su = reinterpret_cast<const float4 *>(wscl + (kSbH + sb) * 8);
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                const float2 x = make_float2(xt[sb * 256 + 64 * i + lane], xt[sb * 256 + 64 * i + 32 + lane]);
+                const float4 s = sg[i], z = su[i];  // d*sc, dmin*m of sub-blocks 2i and 2i+1
+                const float2 wg = __ffma2_rn(make_float2(s.x, s.z), nibbles(qg[32 * i + lane]), make_float2(-s.y, -s.w));
+                const float2 wu = __ffma2_rn(make_float2(z.x, z.z), nibbles(qu[32 * i + lane]), make_float2(-z.y, -z.w));
+                ag = __ffma2_rn(wg, x, ag);
+                au = __ffma2_rn(wu, x, au);
+            }
+        }
+        const float gs = warp_sum(ag.x + ag.y), us = warp_sum(au.x + au.y);
+        if (lane == 0) a.mid[(size_t)p * kLeanF + row] = (gs * sigmoidf_ref(gs)) * us;
+        __syncwarp();  // the scales are rewritten by the next item
+    }
+    if (!grid_barrier(ctr, s_base + 2ull * gridDim.x, err, &s_ok)) return;
+
+    // 3. down rows x route weights, summed over the ten experts, plus the gated shared expert
+    for (int i = tid; i < P * kLeanF / 4; i += kLeanThreads)
+        reinterpret_cast<float4 *>(act)[i] = __ldcg(reinterpret_cast<const float4 *>(a.mid) + i);
+    __syncthreads();
+    const int nk = kTop + (shared ? 1 : 0);
+    for (int it = gw; it < T * kLeanH; it += nw) {
+        const int t = it / kLeanH, row = it % kLeanH;
+        if (s_ids[t * kTop] < 0) {
+            if (lane == 0) a.out[(size_t)t * kLeanH + row] = __int_as_float(0x7fc00000);
+            continue;
+        }
+        uint4 v[kDnPer];
+#pragma unroll
+        for (int i = 0; i < kDnPer; i++) {
+            const int f = lane + 32 * i;
+            if (f < nk * kChF) {
+                const int k = f / kChF, c = f % kChF;
+                const unsigned char *rp = k < kTop ? a.down + ((size_t)s_ids[t * kTop + k] * kLeanH + row) * a.drb
+                                                   : a.sd + (size_t)row * a.drb;
+                v[i] = __ldg(reinterpret_cast<const uint4 *>(rp) + c);
+                reinterpret_cast<uint4 *>(wbuf)[f] = v[i];  // row k at byte k*kChF*16
+            }
+        }
+        __syncwarp();
+        q4k_scales(wbuf, kChF * 16, kSbF, nk * kSbF, wscl);
+        __syncwarp();
+        float acc = 0.0f;
+        for (int k = 0; k < nk; k++) {
+            const int pi = k < kTop ? t * kTop + k : T * kTop + t;
+            const float wk = k < kTop ? s_w[t * kTop + k] : s_sig[t];
+            const float *mt = act + pi * kLeanF;
+            float2 a2 = make_float2(0.0f, 0.0f);
+#pragma unroll
+            for (int sb = 0; sb < kSbF; sb++) {
+                const unsigned char *q = wbuf + k * kChF * 16 + sb * 144 + 16;
+                const float4 *sc = reinterpret_cast<const float4 *>(wscl + (k * kSbF + sb) * 8);
+#pragma unroll
+                for (int i = 0; i < 4; i++) {
+                    const float4 s = sc[i];
+                    const float2 m = make_float2(mt[sb * 256 + 64 * i + lane], mt[sb * 256 + 64 * i + 32 + lane]);
+                    const float2 w = __ffma2_rn(make_float2(s.x, s.z), nibbles(q[32 * i + lane]), make_float2(-s.y, -s.w));
+                    a2 = __ffma2_rn(w, m, a2);
+                }
+            }
+            acc = __fmaf_rn(wk, a2.x + a2.y, acc);
+        }
+        acc = warp_sum(acc);
+        if (lane == 0) a.out[(size_t)t * kLeanH + row] = acc;
+        __syncwarp();
+    }
+}
+
+}  // namespace
+
+namespace nb {
+
+// Taken for 1 or 2 tokens: measured on the 48-layer stack, it gave 626 / 818
+// tokens/s at T = 1 / 2 against 358 / 683 for the tensor-core decode path, but
+// 871 / 931 at T = 3 / 4 against about 1,000 / 1,300 (the kernel itself
+// accepts up to kLeanMaxT tokens).
+constexpr int kLeanDispatchMaxT = 2;
+
+bool lean_supported(const DecArgs &a) {
+    if (a.T < 1 || a.T > kLeanDispatchMaxT || a.H != kLeanH || a.F != kLeanF || a.QG != 12 || a.QD != 12 || !a.router ||
+        a.ep_ranks || a.ep_local)
+        return false;
+    int dev = 0, coop = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, dev);
+    return coop != 0;
+}
+
+int lean_run(const DecArgs &a, cudaStream_t st) {
+    int dev = 0, rc = cudaGetDevice(&dev);
+    if (rc) return rc;
+    rc = cudaFuncSetAttribute(lean_moe_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kLeanSmem);
+    if (rc) return rc;
+    int sms = 0, occ = 0;
+    if ((rc = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev))) return rc;
+    if ((rc = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, lean_moe_kernel, kLeanThreads, kLeanSmem))) return rc;
+    if (occ < 1) return cudaErrorCooperativeLaunchTooLarge;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(sms);  // one CTA per SM, all resident (the grid barriers wait on every CTA)
+    cfg.blockDim = dim3(kLeanThreads);
+    cfg.dynamicSmemBytes = kLeanSmem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, lean_moe_kernel, a);
+}
+
+}  // namespace nb

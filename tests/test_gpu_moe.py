@@ -54,13 +54,13 @@ class Layer:
                self.down.p, self.dt, self.H, self.F, ws.p)
         return out.get(), ws
 
-    def layer(self, x, bias=None):
+    def layer(self, x, bias=None, ws=None):
         L = self.L
         T = x.shape[0]
         dx = L.Device(x)
         out = L.Device.empty((T, self.H), np.float32)
         ids, w = L.Device.empty((T, 10), np.int32), L.Device.empty((T, 10), np.float32)
-        ws = L.workspace(T, self.H, self.F)
+        ws = ws if ws is not None else L.workspace(T, self.H, self.F)
         db = L.Device(bias) if bias is not None else None
         sh = (self.sg.p, self.gt, self.su.p, self.gt, self.sd.p, self.dt, self.sr.p) if self.shared else \
             (None, 0, None, 0, None, 0, None)
@@ -269,6 +269,37 @@ def test_prefill_product_shape(L, ref2560, restate, prod_2560):
     out, ws = prod_2560.routed(x, e_ids, e_w)
     assert_parity(out, oracle_routed(ref2560, prod_2560, x, e_ids, e_w), "product prefill T=2048")
     assert L.status(ws) == (0, T * 10, 512)
+
+
+@pytest.mark.parametrize("T", (1, 2, 3, 4))
+def test_layer_small_batch_single_kernel(L, ref2048, restate, q4k_2048, T):
+    """Small batches: 1 or 2 tokens run the whole layer in one kernel (router,
+    top-10, gate/up, down and combine), 3 and 4 the tensor-core decode path. Ids
+    bit-exact, outputs within tolerance, with the shared expert and a routing
+    bias, over three calls on one workspace (the single kernel's grid-barrier
+    counter carries over). A token with a non-finite input gets a NaN row and is
+    counted as invalid."""
+    rng = np.random.default_rng(600 + T)
+    bias = np.zeros(512, np.float32)
+    bias[rng.permutation(512)] = (-1.1 * np.log(np.arange(512) + 1.0)).astype(np.float32)
+    ws = L.workspace(T, 2048, 512)
+    for call in range(3):
+        x = rng.normal(0, 1, (T, 2048)).astype(np.float32)
+        if call == 2:
+            x[T - 1, 5] = np.nan
+        out, ids, w, _ = q4k_2048.layer(x, bias, ws=ws)
+        n = T if call < 2 else T - 1  # the finite tokens come first; the checker takes only those
+        if n:
+            xg = x[:n]
+            logits = ref2048.matmul(q4k_2048.hrouter.view(np.uint8), 0, 512, 2048, xg) + bias
+            e_out, e_ids, e_w, _ = orc.moe_layer(ref2048, restate, xg, None, q4k_2048.hgate, 12, q4k_2048.hup, 12,
+                                                 q4k_2048.hdown, 12, shared=q4k_2048.shared, logits=logits)
+            np.testing.assert_array_equal(ids[:n], e_ids)
+            assert_parity(out[:n], e_out, f"T={T} call {call}")
+        inv, sel, used = L.status(ws)
+        assert (inv, sel, used) == (T - n, n * 10, len(np.unique(ids[:n])))
+        if call == 2:
+            assert np.isnan(out[T - 1]).all() and (ids[T - 1] == -1).all()
 
 
 def test_layer_zipf_bias(L, ref2048, restate, q4k_2048):
