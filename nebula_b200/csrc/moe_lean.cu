@@ -205,14 +205,14 @@ __global__ void __launch_bounds__(kLeanThreads, 1) lean_moe_kernel(DecArgs a) {
     }
     //    gate/up + SwiGLU: item = (pair p, row); pairs 0..10T-1 routed, 10T.. the shared expert's
     const int P = T * kTop + (shared ? T : 0);
-    for (int it = gw; it < P * kLeanF; it += nw) {
+    // items in order it = gw, gw + nw, ...; the next item's loads are issued before
+    // this item's multiply-adds, so its latency overlaps them
+    auto gu_src = [&](int it, const unsigned char *&g, const unsigned char *&u, int &t) {
         const int p = it / kLeanF, row = it % kLeanF;
-        int t;
-        const unsigned char *g, *u;
         if (p < T * kTop) {
             t = p / kTop;
             const int e = s_ids[p];
-            if (e < 0) continue;  // a token whose logits were not finite: no contributions
+            if (e < 0) return false;  // a token whose logits were not finite: no contributions
             g = a.gate + ((size_t)e * kLeanF + row) * a.grb;
             u = a.up + ((size_t)e * kLeanF + row) * a.grb;
         } else {
@@ -220,15 +220,31 @@ __global__ void __launch_bounds__(kLeanThreads, 1) lean_moe_kernel(DecArgs a) {
             g = a.sg + (size_t)row * a.grb;
             u = a.su + (size_t)row * a.grb;
         }
-        uint4 v[kGuPer];
+        return true;
+    };
+    auto gu_load = [&](const unsigned char *g, const unsigned char *u, uint4 (&v)[kGuPer]) {
 #pragma unroll
         for (int i = 0; i < kGuPer; i++) {
             const int f = lane + 32 * i;
-            if (f < 2 * kChH) {
-                v[i] = __ldg(reinterpret_cast<const uint4 *>(f < kChH ? g : u) + (f < kChH ? f : f - kChH));
-                reinterpret_cast<uint4 *>(wbuf)[f] = v[i];  // gate row at byte 0, up row at kChH*16
-            }
+            if (f < 2 * kChH) v[i] = __ldg(reinterpret_cast<const uint4 *>(f < kChH ? g : u) + (f < kChH ? f : f - kChH));
         }
+    };
+    const int total = P * kLeanF;
+    int it = gw, t = 0;
+    const unsigned char *g = nullptr, *u = nullptr;
+    while (it < total && !gu_src(it, g, u, t)) it += nw;
+    uint4 v[kGuPer];
+    if (it < total) gu_load(g, u, v);
+    while (it < total) {
+#pragma unroll
+        for (int i = 0; i < kGuPer; i++) {
+            const int f = lane + 32 * i;
+            if (f < 2 * kChH) reinterpret_cast<uint4 *>(wbuf)[f] = v[i];  // gate row at byte 0, up row at kChH*16
+        }
+        const int p = it / kLeanF, row = it % kLeanF;
+        int nx = it + nw, tn = 0;
+        while (nx < total && !gu_src(nx, g, u, tn)) nx += nw;
+        if (nx < total) gu_load(g, u, v);
         __syncwarp();
         q4k_scales(wbuf, kChH * 16, kSbH, 2 * kSbH, wscl);
         __syncwarp();
@@ -253,7 +269,9 @@ __global__ void __launch_bounds__(kLeanThreads, 1) lean_moe_kernel(DecArgs a) {
         }
         const float gs = warp_sum(ag.x + ag.y), us = warp_sum(au.x + au.y);
         if (lane == 0) a.mid[(size_t)p * kLeanF + row] = (gs * sigmoidf_ref(gs)) * us;
-        __syncwarp();  // the scales are rewritten by the next item
+        __syncwarp();  // the buffer and the scales are rewritten by the next item
+        it = nx;
+        t = tn;
     }
     if (!grid_barrier(ctr, s_base + 2ull * gridDim.x, err, &s_ok)) return;
 
