@@ -350,14 +350,22 @@ bool lean_supported(const DecArgs &a) {
 int lean_run(const DecArgs &a, cudaStream_t st) {
     int dev = 0, rc = cudaGetDevice(&dev);
     if (rc) return rc;
-    rc = cudaFuncSetAttribute(lean_moe_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kLeanSmem);
-    if (rc) return rc;
-    int sms = 0, occ = 0;
-    if ((rc = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev))) return rc;
-    if ((rc = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, lean_moe_kernel, kLeanThreads, kLeanSmem))) return rc;
-    if (occ < 1) return cudaErrorCooperativeLaunchTooLarge;
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    // once per device: the shared-memory attribute, and the grid (one CTA per SM, all
+    // resident: the grid barriers wait on every CTA)
+    static int grid[64];
+    if (!grid[dev]) {
+        rc = cudaFuncSetAttribute(lean_moe_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kLeanSmem);
+        if (rc) return rc;
+        int sms = 0, occ = 0;
+        if ((rc = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev))) return rc;
+        if ((rc = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, lean_moe_kernel, kLeanThreads, kLeanSmem)))
+            return rc;
+        if (occ < 1) return cudaErrorCooperativeLaunchTooLarge;
+        grid[dev] = sms;
+    }
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(sms);  // one CTA per SM, all resident (the grid barriers wait on every CTA)
+    cfg.gridDim = dim3(grid[dev]);
     cfg.blockDim = dim3(kLeanThreads);
     cfg.dynamicSmemBytes = kLeanSmem;
     cfg.stream = st;
