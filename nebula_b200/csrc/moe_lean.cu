@@ -1,4 +1,6 @@
-// Lean decode layer for batches of 1 or 2 tokens: the whole routed-MoE layer
+// Lean decode layer for batches of 1 or 2 tokens, at hidden 2048 / ffn 512
+// with Q4_K experts and at Nebula's 2560 / 640 with Q4_K gate/up and IQ4_NL
+// down: the whole routed-MoE layer
 // (router GEMV, top-10, gate/up + SwiGLU, down x route weight, combine and the
 // gated shared expert) in ONE cooperative kernel of one CTA per SM.
 //
@@ -36,14 +38,29 @@ using namespace nb;
 
 namespace {
 
-constexpr int kLeanH = 2048, kLeanF = 512;    // the shape this kernel is built for
 constexpr int kLeanThreads = 512, kLeanWarps = kLeanThreads / 32;
 constexpr int kLeanMaxT = 4;
-constexpr int kSbH = kLeanH / 256, kSbF = kLeanF / 256;  // Q4_K superblocks per gate/up row, per down row
-constexpr int kChH = kSbH * 9, kChF = kSbF * 9;          // 16-byte chunks per row
-constexpr int kMaxSb = 2 * kSbH > 11 * kSbF ? 2 * kSbH : 11 * kSbF;  // superblocks of one warp item
-// gate/up: the two rows' chunks over 32 lanes; down: eleven rows' chunks
-constexpr int kGuPer = (2 * kChH + 31) / 32, kDnPer = (11 * kChF + 31) / 32;
+
+constexpr int cmax(int a, int b) { return a > b ? a : b; }
+// One instantiation's shape: hidden H, ffn F, Q4_K gate/up, down Q4_K (QD 12) or IQ4_NL (QD 20).
+template <int H, int F, int QD>
+struct LeanShape {
+    static constexpr int kSbH = H / 256, kChH = kSbH * 9;  // gate/up: Q4_K superblocks, 16-byte chunks per row
+    static constexpr int kDnRow = QD == 12 ? F / 256 * 144 : F / 32 * 18;  // bytes of a down row
+    static constexpr int kSbF = QD == 12 ? F / 256 : 0;     // Q4_K superblocks per down row
+    // down rows are copied 16 bytes at a time (Q4_K), or 8 (IQ4_NL rows are only 8-byte aligned)
+    static constexpr int kDnUnit = QD == 12 ? 16 : 8, kChF = kDnRow / kDnUnit;
+    static constexpr int kMaxSb = cmax(2 * kSbH, 11 * kSbF);  // Q4_K superblocks of one warp item
+    // gate/up: the two rows' chunks over 32 lanes; down: eleven rows' units
+    static constexpr int kGuPer = (2 * kChH + 31) / 32, kDnPer = (11 * kChF + 31) / 32;
+    // shared memory: activations (x [T][H], then mid [P][F]); per warp the superblock
+    // scales and the item's weight rows
+    static constexpr int kActFloats = cmax(kLeanMaxT * H, (kLeanMaxT * kTop + kLeanMaxT) * F);
+    static constexpr int kWBuf = (cmax(2 * kChH * 16, 11 * kDnRow) + 127) / 128 * 128;
+    static constexpr int kSmem = kActFloats * 4 + kLeanWarps * kMaxSb * 8 * 8 + kLeanWarps * kWBuf;
+    static_assert(H % 256 == 0 && F % 256 == 0 || QD == 20, "Q4_K rows");
+    static_assert(kDnRow % kDnUnit == 0 && (2 * kChH * 16) % 16 == 0, "copy units");
+};
 
 __device__ __forceinline__ int ld_acquire_gpu(const int *p) {
     int v;
@@ -111,16 +128,12 @@ __device__ __forceinline__ float warp_sum(float v) {
 
 namespace {
 
-// Shared memory: activations (x [T][H] in phases 1-2, then mid [P][F] in phase 3),
-// and per warp the (d*sc, dmin*m) of the superblocks of its current item.
-constexpr int kActFloats = (kLeanMaxT * kLeanH > (kLeanMaxT * kTop + kLeanMaxT) * kLeanF)
-                               ? kLeanMaxT * kLeanH
-                               : (kLeanMaxT * kTop + kLeanMaxT) * kLeanF;
-// per warp: its item's weight rows (two gate/up rows or eleven down rows, 16-byte chunks)
-constexpr int kWBuf = ((2 * kChH > 11 * kChF ? 2 * kChH : 11 * kChF) * 16 + 127) / 128 * 128;
-constexpr int kLeanSmem = kActFloats * 4 + kLeanWarps * kMaxSb * 8 * 8 + kLeanWarps * kWBuf;
-
+template <int H, int F, int QD>
 __global__ void __launch_bounds__(kLeanThreads, 1) lean_moe_kernel(DecArgs a) {
+    using S = LeanShape<H, F, QD>;
+    constexpr int kLeanH = H, kLeanF = F, kSbH = S::kSbH, kChH = S::kChH, kSbF = S::kSbF, kChF = S::kChF,
+                  kMaxSb = S::kMaxSb, kGuPer = S::kGuPer, kDnPer = S::kDnPer, kActFloats = S::kActFloats,
+                  kWBuf = S::kWBuf;
     extern __shared__ __align__(16) float lsm[];
     float *act = lsm;
     float2 *wscl = reinterpret_cast<float2 *>(lsm + kActFloats) + (threadIdx.x >> 5) * (kMaxSb * 8);
@@ -129,7 +142,9 @@ __global__ void __launch_bounds__(kLeanThreads, 1) lean_moe_kernel(DecArgs a) {
     __shared__ int s_ids[kLeanMaxT * kTop];
     __shared__ float s_w[kLeanMaxT * kTop], s_sig[kLeanMaxT];
     __shared__ int s_ok;
+    __shared__ float s_lut[16];  // IQ4_NL code book
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    if (tid < 16) s_lut[tid] = static_cast<float>(kIq4nl[tid]);
     const int T = a.T, gw = blockIdx.x * kLeanWarps + warp, nw = gridDim.x * kLeanWarps;
     const bool shared = a.sg != nullptr;
     unsigned long long *ctr = &a.ctr->lean_barrier;
@@ -151,17 +166,21 @@ __global__ void __launch_bounds__(kLeanThreads, 1) lean_moe_kernel(DecArgs a) {
         float acc[kLeanMaxT];
 #pragma unroll
         for (int t = 0; t < kLeanMaxT; t++) acc[t] = 0.0f;
+        constexpr int kIter = kLeanH / 32;  // columns per lane
 #pragma unroll
-        for (int h = 0; h < kLeanH / 1024; h++) {
-            float wv[32];  // a row's loads are all in flight before the first multiply-add
+        for (int h = 0; h < kIter; h += 32) {
+            float wv[32];  // 32 of a row's loads in flight before the first multiply-add
 #pragma unroll
-            for (int i = 0; i < 32; i++) wv[i] = __ldg(w + h * 1024 + 32 * i + lane);
+            for (int i = 0; i < 32; i++)
+                if (h + i < kIter) wv[i] = __ldg(w + (h + i) * 32 + lane);
 #pragma unroll
             for (int i = 0; i < 32; i++) {
-                const int k = h * 1024 + 32 * i + lane;
+                if (h + i < kIter) {
+                    const int k = (h + i) * 32 + lane;
 #pragma unroll
-                for (int t = 0; t < kLeanMaxT; t++)
-                    if (t < T) acc[t] = __fmaf_rn(wv[i], act[t * kLeanH + k], acc[t]);
+                    for (int t = 0; t < kLeanMaxT; t++)
+                        if (t < T) acc[t] = __fmaf_rn(wv[i], act[t * kLeanH + k], acc[t]);
+                }
             }
         }
 #pragma unroll
@@ -286,40 +305,70 @@ __global__ void __launch_bounds__(kLeanThreads, 1) lean_moe_kernel(DecArgs a) {
             if (lane == 0) a.out[(size_t)t * kLeanH + row] = __int_as_float(0x7fc00000);
             continue;
         }
-        uint4 v[kDnPer];
-#pragma unroll
-        for (int i = 0; i < kDnPer; i++) {
-            const int f = lane + 32 * i;
-            if (f < nk * kChF) {
-                const int k = f / kChF, c = f % kChF;
-                const unsigned char *rp = k < kTop ? a.down + ((size_t)s_ids[t * kTop + k] * kLeanH + row) * a.drb
-                                                   : a.sd + (size_t)row * a.drb;
-                v[i] = __ldg(reinterpret_cast<const uint4 *>(rp) + c);
-                reinterpret_cast<uint4 *>(wbuf)[f] = v[i];  // row k at byte k*kChF*16
-            }
-        }
-        __syncwarp();
-        q4k_scales(wbuf, kChF * 16, kSbF, nk * kSbF, wscl);
-        __syncwarp();
         float acc = 0.0f;
-        for (int k = 0; k < nk; k++) {
-            const int pi = k < kTop ? t * kTop + k : T * kTop + t;
-            const float wk = k < kTop ? s_w[t * kTop + k] : s_sig[t];
-            const float *mt = act + pi * kLeanF;
-            float2 a2 = make_float2(0.0f, 0.0f);
+        if constexpr (QD == 12) {
+            uint4 v[kDnPer];
 #pragma unroll
-            for (int sb = 0; sb < kSbF; sb++) {
-                const unsigned char *q = wbuf + k * kChF * 16 + sb * 144 + 16;
-                const float4 *sc = reinterpret_cast<const float4 *>(wscl + (k * kSbF + sb) * 8);
-#pragma unroll
-                for (int i = 0; i < 4; i++) {
-                    const float4 s = sc[i];
-                    const float2 m = make_float2(mt[sb * 256 + 64 * i + lane], mt[sb * 256 + 64 * i + 32 + lane]);
-                    const float2 w = __ffma2_rn(make_float2(s.x, s.z), nibbles(q[32 * i + lane]), make_float2(-s.y, -s.w));
-                    a2 = __ffma2_rn(w, m, a2);
+            for (int i = 0; i < kDnPer; i++) {
+                const int f = lane + 32 * i;
+                if (f < nk * kChF) {
+                    const int k = f / kChF, c = f % kChF;
+                    const unsigned char *rp = k < kTop ? a.down + ((size_t)s_ids[t * kTop + k] * kLeanH + row) * a.drb
+                                                       : a.sd + (size_t)row * a.drb;
+                    v[i] = __ldg(reinterpret_cast<const uint4 *>(rp) + c);
+                    reinterpret_cast<uint4 *>(wbuf)[f] = v[i];  // row k at byte k*kChF*16
                 }
             }
-            acc = __fmaf_rn(wk, a2.x + a2.y, acc);
+            __syncwarp();
+            q4k_scales(wbuf, kChF * 16, kSbF, nk * kSbF, wscl);
+            __syncwarp();
+            for (int k = 0; k < nk; k++) {
+                const int pi = k < kTop ? t * kTop + k : T * kTop + t;
+                const float wk = k < kTop ? s_w[t * kTop + k] : s_sig[t];
+                const float *mt = act + pi * kLeanF;
+                float2 a2 = make_float2(0.0f, 0.0f);
+#pragma unroll
+                for (int sb = 0; sb < kSbF; sb++) {
+                    const unsigned char *q = wbuf + k * kChF * 16 + sb * 144 + 16;
+                    const float4 *sc = reinterpret_cast<const float4 *>(wscl + (k * kSbF + sb) * 8);
+#pragma unroll
+                    for (int i = 0; i < 4; i++) {
+                        const float4 s = sc[i];
+                        const float2 m = make_float2(mt[sb * 256 + 64 * i + lane], mt[sb * 256 + 64 * i + 32 + lane]);
+                        const float2 w = __ffma2_rn(make_float2(s.x, s.z), nibbles(q[32 * i + lane]), make_float2(-s.y, -s.w));
+                        a2 = __ffma2_rn(w, m, a2);
+                    }
+                }
+                acc = __fmaf_rn(wk, a2.x + a2.y, acc);
+            }
+        } else {
+            // IQ4_NL rows: 8-byte units; lane j takes value j of every 32-value block
+#pragma unroll
+            for (int i = 0; i < kDnPer; i++) {
+                const int f = lane + 32 * i;
+                if (f < nk * kChF) {
+                    const int k = f / kChF, c = f % kChF;
+                    const unsigned char *rp = k < kTop ? a.down + ((size_t)s_ids[t * kTop + k] * kLeanH + row) * a.drb
+                                                       : a.sd + (size_t)row * a.drb;
+                    reinterpret_cast<uint2 *>(wbuf)[f] = __ldg(reinterpret_cast<const uint2 *>(rp) + c);
+                }
+            }
+            __syncwarp();
+            for (int k = 0; k < nk; k++) {
+                const int pi = k < kTop ? t * kTop + k : T * kTop + t;
+                const float wk = k < kTop ? s_w[t * kTop + k] : s_sig[t];
+                const float *mt = act + pi * kLeanF;
+                const unsigned char *rw = wbuf + k * S::kDnRow;
+                float a2 = 0.0f;
+#pragma unroll 4
+                for (int b = 0; b < kLeanF / 32; b++) {
+                    const unsigned char *blk = rw + b * 18;
+                    const unsigned q = blk[2 + (lane & 15)];
+                    const float wv = half_at(blk) * s_lut[lane < 16 ? (q & 15u) : (q >> 4)];  // d * code, exact
+                    a2 = __fmaf_rn(wv, mt[b * 32 + lane], a2);
+                }
+                acc = __fmaf_rn(wk, a2, acc);
+            }
         }
         acc = warp_sum(acc);
         if (lane == 0) a.out[(size_t)t * kLeanH + row] = acc;
@@ -327,19 +376,55 @@ __global__ void __launch_bounds__(kLeanThreads, 1) lean_moe_kernel(DecArgs a) {
     }
 }
 
+// Taken for 1 or 2 tokens: measured on the 48-layer stack (2048/512, Q4_K), it gave
+// 643 / 838 tokens/s at T = 1 / 2 against 358 / 683 for the tensor-core decode
+// path, but 871 / 931 at T = 3 / 4 against about 1,000 / 1,300.
+constexpr int kLeanDispatchMaxT = 2;
+
+bool lean_shape(const DecArgs &a, int &which) {
+    if (a.QG != 12) return false;
+    if (a.H == 2048 && a.F == 512 && a.QD == 12) which = 0;       // the benchmark configurations
+    else if (a.H == 2560 && a.F == 640 && a.QD == 20) which = 1;  // Nebula's production mix
+    else return false;
+    return true;
+}
+
+template <int H, int F, int QD>
+int lean_launch(const DecArgs &a, cudaStream_t st, int dev) {
+    using S = LeanShape<H, F, QD>;
+    auto k = lean_moe_kernel<H, F, QD>;
+    // once per device: the shared-memory attribute, and the grid (one CTA per SM, all
+    // resident: the grid barriers wait on every CTA)
+    static int grid[64];
+    if (!grid[dev]) {
+        int rc = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kSmem);
+        if (rc) return rc;
+        int sms = 0, occ = 0;
+        if ((rc = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev))) return rc;
+        if ((rc = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, k, kLeanThreads, S::kSmem))) return rc;
+        if (occ < 1) return cudaErrorCooperativeLaunchTooLarge;
+        grid[dev] = sms;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid[dev]);
+    cfg.blockDim = dim3(kLeanThreads);
+    cfg.dynamicSmemBytes = S::kSmem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, k, a);
+}
+
 }  // namespace
 
 namespace nb {
 
-// Taken for 1 or 2 tokens: measured on the 48-layer stack, it gave 626 / 818
-// tokens/s at T = 1 / 2 against 358 / 683 for the tensor-core decode path, but
-// 871 / 931 at T = 3 / 4 against about 1,000 / 1,300 (the kernel itself
-// accepts up to kLeanMaxT tokens).
-constexpr int kLeanDispatchMaxT = 2;
-
 bool lean_supported(const DecArgs &a) {
-    if (a.T < 1 || a.T > kLeanDispatchMaxT || a.H != kLeanH || a.F != kLeanF || a.QG != 12 || a.QD != 12 || !a.router ||
-        a.ep_ranks || a.ep_local)
+    int which = 0;
+    if (a.T < 1 || a.T > kLeanDispatchMaxT || !lean_shape(a, which) || !a.router || a.ep_ranks || a.ep_local)
         return false;
     int dev = 0, coop = 0;
     cudaGetDevice(&dev);
@@ -348,33 +433,11 @@ bool lean_supported(const DecArgs &a) {
 }
 
 int lean_run(const DecArgs &a, cudaStream_t st) {
-    int dev = 0, rc = cudaGetDevice(&dev);
+    int dev = 0, which = 0, rc = cudaGetDevice(&dev);
     if (rc) return rc;
     if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
-    // once per device: the shared-memory attribute, and the grid (one CTA per SM, all
-    // resident: the grid barriers wait on every CTA)
-    static int grid[64];
-    if (!grid[dev]) {
-        rc = cudaFuncSetAttribute(lean_moe_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kLeanSmem);
-        if (rc) return rc;
-        int sms = 0, occ = 0;
-        if ((rc = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev))) return rc;
-        if ((rc = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, lean_moe_kernel, kLeanThreads, kLeanSmem)))
-            return rc;
-        if (occ < 1) return cudaErrorCooperativeLaunchTooLarge;
-        grid[dev] = sms;
-    }
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(grid[dev]);
-    cfg.blockDim = dim3(kLeanThreads);
-    cfg.dynamicSmemBytes = kLeanSmem;
-    cfg.stream = st;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeCooperative;
-    attr[0].val.cooperative = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, lean_moe_kernel, a);
+    if (!lean_shape(a, which)) return cudaErrorInvalidValue;
+    return which == 0 ? lean_launch<2048, 512, 12>(a, st, dev) : lean_launch<2560, 640, 20>(a, st, dev);
 }
 
 }  // namespace nb
