@@ -104,10 +104,12 @@ __device__ bool grid_barrier(unsigned long long *ctr, unsigned long long target,
 // sub-block) per lane and step: scl[h*8 + g] for superblock h = r*sbs + sb.
 __device__ __forceinline__ void q4k_scales(const unsigned char *buf, int rb, int sbs, int nh, float2 *scl) {
     for (int pg = threadIdx.x & 31; pg < nh * 8; pg += 32) {
-        const int h = pg >> 3, g = pg & 7;
+        const int h = pg >> 3, g = pg & 7, j = g & 3;
         const unsigned char *hd = buf + (h / sbs) * rb + (h % sbs) * 144;
-        int sc, m;
-        k_scale_min(hd + 4, g, sc, m);
+        // the 6-bit scale and min of sub-block g (k_scale_min's layout), selected without branches
+        const int b0 = hd[4 + j], b4 = hd[8 + j], b8 = hd[12 + j];
+        const int sc = g < 4 ? (b0 & 63) : ((b8 & 15) | ((b0 >> 6) << 4));
+        const int m = g < 4 ? (b4 & 63) : ((b8 >> 4) | ((b4 >> 6) << 4));
         scl[pg] = make_float2(half_at(hd) * static_cast<float>(sc), half_at(hd + 2) * static_cast<float>(m));
     }
 }
