@@ -170,13 +170,13 @@ __global__ void __launch_bounds__(kLeanThreads, 1) lean_moe_kernel(DecArgs a) {
         for (int t = 0; t < kLeanMaxT; t++) acc[t] = 0.0f;
         constexpr int kIter = kLeanH / 32;  // columns per lane
 #pragma unroll
-        for (int h = 0; h < kIter; h += 32) {
-            float wv[32];  // 32 of a row's loads in flight before the first multiply-add
+        for (int h = 0; h < kIter; h += 64) {
+            float wv[64];  // up to 64 of a row's loads in flight before the first multiply-add
 #pragma unroll
-            for (int i = 0; i < 32; i++)
+            for (int i = 0; i < 64; i++)
                 if (h + i < kIter) wv[i] = __ldg(w + (h + i) * 32 + lane);
 #pragma unroll
-            for (int i = 0; i < 32; i++) {
+            for (int i = 0; i < 64; i++) {
                 if (h + i < kIter) {
                     const int k = (h + i) * 32 + lane;
 #pragma unroll
@@ -207,21 +207,25 @@ __global__ void __launch_bounds__(kLeanThreads, 1) lean_moe_kernel(DecArgs a) {
             a.ids[tid] = s_ids[tid];
             a.wts[tid] = s_w[tid];
         }
-        if (tid == 0) {  // status words: pairs computed, distinct experts, tokens with NaN rows
-            int pairs = 0, used = 0, bad = 0;
-            for (int t = 0; t < T; t++) {
-                if (s_ids[t * kTop] < 0) bad++;
-                else pairs += kTop;
-            }
-            for (int i = 0; i < T * kTop; i++) {
+        if (warp == 0) {  // status words: pairs computed, distinct experts, tokens with NaN rows
+            int first = 0;    // ids that no earlier slot holds, one slot per lane and step
+            for (int i = lane; i < T * kTop; i += 32) {
                 const int e = s_ids[i];
-                bool first = e >= 0;
-                for (int j = 0; j < i && first; j++) first = s_ids[j] != e;
-                used += first;
+                bool f = e >= 0;
+                for (int j = 0; j < i && f; j++) f = s_ids[j] != e;
+                first += f;
             }
-            a.hdr->n_pairs = pairs;
-            a.hdr->n_used = used;
-            a.hdr->invalid_tokens = bad;
+            const int used = (int)__reduce_add_sync(0xffffffffu, (unsigned)first);
+            if (lane == 0) {
+                int pairs = 0, bad = 0;
+                for (int t = 0; t < T; t++) {
+                    if (s_ids[t * kTop] < 0) bad++;
+                    else pairs += kTop;
+                }
+                a.hdr->n_pairs = pairs;
+                a.hdr->n_used = used;
+                a.hdr->invalid_tokens = bad;
+            }
         }
     }
     //    gate/up + SwiGLU: item = (pair p, row); pairs 0..10T-1 routed, 10T.. the shared expert's
