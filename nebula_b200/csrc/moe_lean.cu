@@ -348,7 +348,9 @@ __global__ void __launch_bounds__(kLeanThreads, 1) lean_moe_kernel(DecArgs a) {
                 acc = __fmaf_rn(wk, a2.x + a2.y, acc);
             }
         } else {
-            // IQ4_NL rows: 8-byte units; lane j takes value j of every 32-value block
+            // IQ4_NL rows: 8-byte units. Half-warp h takes block 2m+h of each pair of
+            // blocks; lane j of it reads code byte j (values j and j+16 of the block),
+            // the two halves loading their activations in orders that use different banks
 #pragma unroll
             for (int i = 0; i < kDnPer; i++) {
                 const int f = lane + 32 * i;
@@ -366,12 +368,17 @@ __global__ void __launch_bounds__(kLeanThreads, 1) lean_moe_kernel(DecArgs a) {
                 const float *mt = act + pi * kLeanF;
                 const unsigned char *rw = wbuf + k * S::kDnRow;
                 float a2 = 0.0f;
-#pragma unroll 4
-                for (int b = 0; b < kLeanF / 32; b++) {
+                const int hb = lane >> 4, j = lane & 15;
+#pragma unroll 5
+                for (int m = 0; m < kLeanF / 64; m++) {
+                    const int b = 2 * m + hb;
                     const unsigned char *blk = rw + b * 18;
-                    const unsigned q = blk[2 + (lane & 15)];
-                    const float wv = half_at(blk) * s_lut[lane < 16 ? (q & 15u) : (q >> 4)];  // d * code, exact
-                    a2 = __fmaf_rn(wv, mt[b * 32 + lane], a2);
+                    const unsigned q = blk[2 + j];
+                    const float d = half_at(blk);
+                    // first the value at j + 16*hb (low nibble for h = 0, high for h = 1), then the other
+                    const float w1 = d * s_lut[(q >> (4 * hb)) & 15u], w2 = d * s_lut[(q >> (4 - 4 * hb)) & 15u];
+                    a2 = __fmaf_rn(w1, mt[b * 32 + j + 16 * hb], a2);
+                    a2 = __fmaf_rn(w2, mt[b * 32 + j + 16 - 16 * hb], a2);
                 }
                 acc = __fmaf_rn(wk, a2, acc);
             }
