@@ -393,10 +393,11 @@ __global__ void __launch_bounds__(LeanShape<H, F, QD>::kThreads, 1) lean_moe_ker
     }
 }
 
-// Taken for 1 or 2 tokens: measured on the 48-layer stack (2048/512, Q4_K), it gave
-// 643 / 838 tokens/s at T = 1 / 2 against 358 / 683 for the tensor-core decode
-// path, but 871 / 931 at T = 3 / 4 against about 1,000 / 1,300.
-constexpr int kLeanDispatchMaxT = 2;
+// Taken for 1 or 2 tokens: measured on the 48-layer stack (2048/512, Q4_K), it gives
+// 692 / 936 tokens/s at T = 1 / 2 against 358 / 683 for the tensor-core decode path;
+// an earlier build that also took 3 and 4 tokens gave 871 / 931 there, against about
+// 1,000 / 1,300 for the tensor-core path.
+constexpr int kLeanDispatchMaxT = kLeanMaxT;
 
 bool lean_shape(const DecArgs &a, int &which) {
     if (a.QG != 12) return false;
