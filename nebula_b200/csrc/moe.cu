@@ -1266,7 +1266,11 @@ extern "C" int qg_moe_layer(float *out, int *ids_out, float *weights_out, const 
         a.sd = static_cast<const unsigned char *>(sd);
         if (lean_supported(a)) {
             Span sp(kLean, st);
-            return lean_run(a, st);
+            const int rc = lean_run(a, st);
+            // a device that cannot hold every CTA of the cooperative launch at once takes
+            // the multi-kernel path below instead
+            if (rc != cudaErrorCooperativeLaunchTooLarge) return rc;
+            (void)cudaGetLastError();
         }
         return dec_run_timed(a, st);
     }
