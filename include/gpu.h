@@ -220,7 +220,8 @@ int qg_moe_status(const void *workspace, int *invalid_tokens, int *selected, int
  * recorded durations of one phase - 0 router GEMV, 1 top-10, 2 plan,
  * 3 gate/up, 4 down, 5 combine, 6 fused expert kernel (gate/up, down and
  * combine in one launch), 7 fused router/top-10/plan kernel of the decode
- * path, 8 the single-kernel layer of batches of 1 or 2 tokens - and
+ * path, 8 the single-kernel layer of small batches (1 or 2 tokens at
+ * hidden 2048 / ffn 512, 1 to 4 at 2560 / 640) - and
  * synchronises the device. While profiling, the decode path's
  * two kernels run without programmatic overlap. */
 int qg_moe_profile(int enable);

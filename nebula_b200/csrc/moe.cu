@@ -46,7 +46,7 @@ namespace {
 // Only eager launches on the legacy stream are timed; graph captures are not.
 // kExpertsFused: one kernel doing gate/up, SwiGLU, down and the combine;
 // kDecodeRouter: one kernel doing the router GEMV, top-10 and the plan.
-// kLean: the whole layer in one kernel (batches of 1 or 2 tokens).
+// kLean: the whole layer in one kernel (batches of 1 to 4 tokens).
 enum Phase { kRouter, kRoute, kPlan, kGateUp, kDown, kCombine, kExpertsFused, kDecodeRouter, kLean, kPhases };
 struct Profiler {
     bool on = false;

@@ -72,9 +72,9 @@ bool dec_supported(int T, int H, int F, int QG, int QD);
 // split != null (profiling): recorded between the router/plan kernel and the
 // expert kernel, which is then launched without programmatic overlap.
 int dec_run(const DecArgs &a, cudaStream_t st, cudaEvent_t split = nullptr);
-// The lean single-kernel layer (moe_lean.cu): 1 or 2 tokens, router given, one
-// GPU; hidden 2048 / ffn 512 with Q4_K experts, or 2560 / 640 with Q4_K gate/up
-// and IQ4_NL down.
+// The lean single-kernel layer (moe_lean.cu): router given, one GPU; 1 or 2
+// tokens at hidden 2048 / ffn 512 with Q4_K experts, 1 to 4 at 2560 / 640 with
+// Q4_K gate/up and IQ4_NL down.
 bool lean_supported(const DecArgs &a);
 int lean_run(const DecArgs &a, cudaStream_t st);
 

@@ -1,6 +1,6 @@
-// Lean decode layer for batches of 1 or 2 tokens, at hidden 2048 / ffn 512
-// with Q4_K experts and at Nebula's 2560 / 640 with Q4_K gate/up and IQ4_NL
-// down: the whole routed-MoE layer
+// Lean decode layer for batches of 1 or 2 tokens at hidden 2048 / ffn 512 with
+// Q4_K experts, and of 1 to 4 tokens at Nebula's 2560 / 640 with Q4_K gate/up and
+// IQ4_NL down: the whole routed-MoE layer
 // (router GEMV, top-10, gate/up + SwiGLU, down x route weight, combine and the
 // gated shared expert) in ONE cooperative kernel of one CTA per SM.
 //
@@ -38,7 +38,6 @@ using namespace nb;
 
 namespace {
 
-constexpr int kLeanMaxT = 2;  // tokens the kernel takes
 
 constexpr int cmax(int a, int b) { return a > b ? a : b; }
 // One instantiation's shape: hidden H, ffn F, Q4_K gate/up, down Q4_K (QD 12) or IQ4_NL (QD 20).
@@ -48,28 +47,33 @@ struct LeanShape {
     // IQ4_NL down, whose per-value decoding gains from more warps to hide latency (measured:
     // 768 threads made the 2560/640 layer 18% faster at T=1 and the 2048/512 one 5% slower)
     static constexpr int kThreads = QD == 20 ? 768 : 512, kWarps = kThreads / 32;
+    // tokens the layer takes here: 4 for the 2560/640 mix, 2 for 2048/512, where the
+    // tensor-core decode path is faster from 3 tokens on. Each shape has an instance
+    // for up to 2 tokens and the mix one for 3 or 4 (kernel parameter MT): sized for
+    // 4, the T = 1 and 2 launches measured 2-3 % slower
+    static constexpr int kMaxT = QD == 20 ? 4 : 2;
     static constexpr int kSbH = H / 256, kChH = kSbH * 9;  // gate/up: Q4_K superblocks, 16-byte chunks per row
     static constexpr int kDnRow = QD == 12 ? F / 256 * 144 : F / 32 * 18;  // bytes of a down row
     static constexpr int kSbF = QD == 12 ? F / 256 : 0;     // Q4_K superblocks per down row
     // down rows are copied 16 bytes at a time (Q4_K), or 8 (IQ4_NL rows are only 8-byte aligned)
     static constexpr int kDnUnit = QD == 12 ? 16 : 8, kChF = kDnRow / kDnUnit;
-    static constexpr int kMaxSb = cmax(2 * kSbH, 11 * kSbF);  // Q4_K superblocks of one warp item
     // gate/up: the two rows' chunks over 32 lanes; down: eleven rows' units
     static constexpr int kGuPer = (2 * kChH + 31) / 32, kDnPer = (11 * kChF + 31) / 32;
-    // shared memory: activations (x [T][H], then mid [P][F]); per warp the superblock
-    // scales and the item's weight rows
-    static constexpr int kActFloats = cmax(kLeanMaxT * H, (kLeanMaxT * kTop + kLeanMaxT) * F);
-    static constexpr int kWBuf = (cmax(2 * kChH * 16, 11 * kDnRow) + 127) / 128 * 128;
-    static constexpr int kSmem = kActFloats * 4 + kWarps * kMaxSb * 8 * 8 + kWarps * kWBuf;
+    // shared memory: activations (x [T][H], then mid [P][F]) for the launch's T tokens,
+    // then one region per warp. Each launch asks for only what its T needs: the rest of
+    // the SM's 256 KB stays L1, which holds the weight loads in flight
+    static constexpr __host__ __device__ int act_floats(int t) { return cmax(t * H, (t * kTop + t) * F); }
+    // a warp's region holds its item's weight rows, then their Q4_K superblock scales
+    // (gate/up and down items never overlap in time, so the two phases share it)
+    static constexpr int kGuRows = 2 * kChH * 16, kDnRows = 11 * kDnRow;
+    static constexpr int kWBuf = (cmax(kGuRows + 2 * kSbH * 64, kDnRows + 11 * kSbF * 64) + 127) / 128 * 128;
+    static constexpr __host__ __device__ int smem(int t) { return act_floats(t) * 4 + kWarps * kWBuf; }
+    static_assert(kGuRows % 16 == 0 && (kDnRows % 16 == 0 || QD == 20), "scales 16-byte aligned");
+    static_assert(smem(kMaxT) <= 226 * 1024, "one CTA per SM, with room for the static arrays");
+    static_assert(H % 32 == 0 && F % 32 == 0, "warp regions 128-byte aligned for every T");
     static_assert(H % 256 == 0 && F % 256 == 0 || QD == 20, "Q4_K rows");
     static_assert(kDnRow % kDnUnit == 0 && (2 * kChH * 16) % 16 == 0, "copy units");
 };
-
-__device__ __forceinline__ int ld_acquire_gpu(const int *p) {
-    int v;
-    asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
-}
 
 // Grid-wide barrier over the resident CTAs (cooperative launch) on one 64-bit
 // counter that only grows: every CTA adds 1 per barrier with a non-returning
@@ -133,18 +137,70 @@ __device__ __forceinline__ float warp_sum(float v) {
 
 namespace {
 
-template <int H, int F, int QD>
+// Router GEMV (and the shared-gate row) for NT tokens: warp gw takes rows gw, gw + nw, ...;
+// lane j adds k = j, j+32, ... in order and the lanes are summed by lane_tree, the
+// reference's order (qwen/gpu.cu:89-92).
+template <int NT, int H>
+__device__ __forceinline__ void router_rows(const DecArgs &a, const float *act, int gw, int nw, int lane) {
+    const int rrows = kExperts + (a.s_router ? 1 : 0);
+    for (int row = gw; row < rrows; row += nw) {
+        const float *w = row < kExperts ? a.router + (size_t)row * H : a.s_router;
+        float acc[NT];
+#pragma unroll
+        for (int t = 0; t < NT; t++) acc[t] = 0.0f;
+        constexpr int kIter = H / 32;  // columns per lane
+#pragma unroll
+        for (int h = 0; h < kIter; h += 64) {
+            float wv[64];  // up to 64 of a row's loads in flight before the first multiply-add
+#pragma unroll
+            for (int i = 0; i < 64; i++)
+                if (h + i < kIter) wv[i] = __ldg(w + (h + i) * 32 + lane);
+#pragma unroll
+            for (int i = 0; i < 64; i++) {
+                if (h + i < kIter) {
+                    const int k = (h + i) * 32 + lane;
+#pragma unroll
+                    for (int t = 0; t < NT; t++) acc[t] = __fmaf_rn(wv[i], act[t * H + k], acc[t]);
+                }
+            }
+        }
+#pragma unroll
+        for (int t = 0; t < NT; t++) {
+            const float s = lane_tree(acc[t]);
+            if (lane == 0) {
+                if (row < kExperts) a.logits[t * kExperts + row] = s;
+                else a.sgate[t] = s;
+            }
+        }
+    }
+}
+
+// router_rows<T> for the runtime T in 1..NT
+template <int NT, int H>
+__device__ __forceinline__ void router_rows_upto(const DecArgs &a, const float *act, int T, int gw, int nw, int lane) {
+    if constexpr (NT > 1) {
+        if (T < NT) {
+            router_rows_upto<NT - 1, H>(a, act, T, gw, nw, lane);
+            return;
+        }
+    }
+    router_rows<NT, H>(a, act, gw, nw, lane);
+}
+
+template <int H, int F, int QD, int MT>
 __global__ void __launch_bounds__(LeanShape<H, F, QD>::kThreads, 1) lean_moe_kernel(DecArgs a) {
     using S = LeanShape<H, F, QD>;
     constexpr int kLeanThreads = S::kThreads, kLeanWarps = S::kWarps;
     constexpr int kLeanH = H, kLeanF = F, kSbH = S::kSbH, kChH = S::kChH, kSbF = S::kSbF, kChF = S::kChF,
-                  kMaxSb = S::kMaxSb, kGuPer = S::kGuPer, kDnPer = S::kDnPer, kActFloats = S::kActFloats,
+                  kGuPer = S::kGuPer, kDnPer = S::kDnPer,
                   kWBuf = S::kWBuf;
     extern __shared__ __align__(16) float lsm[];
     float *act = lsm;
-    float2 *wscl = reinterpret_cast<float2 *>(lsm + kActFloats) + (threadIdx.x >> 5) * (kMaxSb * 8);
-    unsigned char *wbuf = reinterpret_cast<unsigned char *>(lsm + kActFloats) + kLeanWarps * kMaxSb * 8 * 8 +
-                          (threadIdx.x >> 5) * kWBuf;
+    static_assert(MT >= 1 && MT <= S::kMaxT, "token limit of the instance");
+    constexpr int kLeanMaxT = MT;
+    unsigned char *wbuf = reinterpret_cast<unsigned char *>(lsm + S::act_floats(a.T)) + (threadIdx.x >> 5) * kWBuf;
+    float2 *wscl_gu = reinterpret_cast<float2 *>(wbuf + S::kGuRows);  // scales after the rows of each phase
+    float2 *wscl_dn = reinterpret_cast<float2 *>(wbuf + S::kDnRows);
     __shared__ int s_ids[kLeanMaxT * kTop];
     __shared__ float s_w[kLeanMaxT * kTop], s_sig[kLeanMaxT];
     __shared__ int s_ok;
@@ -165,41 +221,8 @@ __global__ void __launch_bounds__(LeanShape<H, F, QD>::kThreads, 1) lean_moe_ker
         reinterpret_cast<float4 *>(act)[i] = __ldg(reinterpret_cast<const float4 *>(a.x) + i);
     __syncthreads();
 
-    // 1. router GEMV (and the shared-gate row): lane j adds k = j, j+32, ... in order
-    const int rrows = kExperts + (a.s_router ? 1 : 0);
-    for (int row = gw; row < rrows; row += nw) {
-        const float *w = row < kExperts ? a.router + (size_t)row * kLeanH : a.s_router;
-        float acc[kLeanMaxT];
-#pragma unroll
-        for (int t = 0; t < kLeanMaxT; t++) acc[t] = 0.0f;
-        constexpr int kIter = kLeanH / 32;  // columns per lane
-#pragma unroll
-        for (int h = 0; h < kIter; h += 64) {
-            float wv[64];  // up to 64 of a row's loads in flight before the first multiply-add
-#pragma unroll
-            for (int i = 0; i < 64; i++)
-                if (h + i < kIter) wv[i] = __ldg(w + (h + i) * 32 + lane);
-#pragma unroll
-            for (int i = 0; i < 64; i++) {
-                if (h + i < kIter) {
-                    const int k = (h + i) * 32 + lane;
-#pragma unroll
-                    for (int t = 0; t < kLeanMaxT; t++)
-                        if (t < T) acc[t] = __fmaf_rn(wv[i], act[t * kLeanH + k], acc[t]);
-                }
-            }
-        }
-#pragma unroll
-        for (int t = 0; t < kLeanMaxT; t++) {
-            if (t < T) {
-                const float s = lane_tree(acc[t]);
-                if (lane == 0) {
-                    if (row < kExperts) a.logits[t * kExperts + row] = s;
-                    else a.sgate[t] = s;
-                }
-            }
-        }
-    }
+    // 1. router GEMV (and the shared-gate row), compiled for the launch's token count
+    router_rows_upto<MT, H>(a, act, T, gw, nw, lane);
     if (!grid_barrier(ctr, s_base + gridDim.x, err, &s_ok)) return;
 
     // 2. top-10 of every token, in every CTA
@@ -275,7 +298,7 @@ __global__ void __launch_bounds__(LeanShape<H, F, QD>::kThreads, 1) lean_moe_ker
         while (nx < total && !gu_src(nx, g, u, tn)) nx += nw;
         if (nx < total) gu_load(g, u, v);
         __syncwarp();
-        q4k_scales(wbuf, kChH * 16, kSbH, 2 * kSbH, wscl);
+        q4k_scales(wbuf, kChH * 16, kSbH, 2 * kSbH, wscl_gu);
         __syncwarp();
         // lane j takes byte j of every 32-byte q block: its activations are consecutive
         // across lanes, and each is loaded once for the gate and the up row
@@ -284,8 +307,8 @@ __global__ void __launch_bounds__(LeanShape<H, F, QD>::kThreads, 1) lean_moe_ker
 #pragma unroll 2
         for (int sb = 0; sb < kSbH; sb++) {
             const unsigned char *qg = wbuf + sb * 144 + 16, *qu = qg + kChH * 16;
-            const float4 *sg = reinterpret_cast<const float4 *>(wscl + sb * 8);
-            const float4 *su = reinterpret_cast<const float4 *>(wscl + (kSbH + sb) * 8);
+            const float4 *sg = reinterpret_cast<const float4 *>(wscl_gu + sb * 8);
+            const float4 *su = reinterpret_cast<const float4 *>(wscl_gu + (kSbH + sb) * 8);
 #pragma unroll
             for (int i = 0; i < 4; i++) {
                 const float2 x = make_float2(xt[sb * 256 + 64 * i + lane], xt[sb * 256 + 64 * i + 32 + lane]);
@@ -330,7 +353,7 @@ __global__ void __launch_bounds__(LeanShape<H, F, QD>::kThreads, 1) lean_moe_ker
                 }
             }
             __syncwarp();
-            q4k_scales(wbuf, kChF * 16, kSbF, nk * kSbF, wscl);
+            q4k_scales(wbuf, kChF * 16, kSbF, nk * kSbF, wscl_dn);
             __syncwarp();
             for (int k = 0; k < nk; k++) {
                 const int pi = k < kTop ? t * kTop + k : T * kTop + t;
@@ -340,7 +363,7 @@ __global__ void __launch_bounds__(LeanShape<H, F, QD>::kThreads, 1) lean_moe_ker
 #pragma unroll
                 for (int sb = 0; sb < kSbF; sb++) {
                     const unsigned char *q = wbuf + k * kChF * 16 + sb * 144 + 16;
-                    const float4 *sc = reinterpret_cast<const float4 *>(wscl + (k * kSbF + sb) * 8);
+                    const float4 *sc = reinterpret_cast<const float4 *>(wscl_dn + (k * kSbF + sb) * 8);
 #pragma unroll
                     for (int i = 0; i < 4; i++) {
                         const float4 s = sc[i];
@@ -393,11 +416,10 @@ __global__ void __launch_bounds__(LeanShape<H, F, QD>::kThreads, 1) lean_moe_ker
     }
 }
 
-// Taken for 1 or 2 tokens: measured on the 48-layer stack (2048/512, Q4_K), it gives
-// 692 / 936 tokens/s at T = 1 / 2 against 358 / 683 for the tensor-core decode path;
-// an earlier build that also took 3 and 4 tokens gave 871 / 931 there, against about
-// 1,000 / 1,300 for the tensor-core path.
-constexpr int kLeanDispatchMaxT = kLeanMaxT;
+// Taken up to each shape's kMaxT tokens. Measured on the 48-layer stack (2048/512,
+// Q4_K) it gives 692 / 936 tokens/s at T = 1 / 2 against 358 / 683 for the
+// tensor-core decode path; an earlier build that also took 3 and 4 tokens gave
+// 871 / 931 there, against about 1,000 / 1,300 for the tensor-core path.
 
 bool lean_shape(const DecArgs &a, int &which) {
     if (a.QG != 12) return false;
@@ -407,26 +429,26 @@ bool lean_shape(const DecArgs &a, int &which) {
     return true;
 }
 
-template <int H, int F, int QD>
+template <int H, int F, int QD, int MT>
 int lean_launch(const DecArgs &a, cudaStream_t st, int dev) {
     using S = LeanShape<H, F, QD>;
-    auto k = lean_moe_kernel<H, F, QD>;
+    auto k = lean_moe_kernel<H, F, QD, MT>;
     // once per device: the shared-memory attribute, and the grid (one CTA per SM, all
     // resident: the grid barriers wait on every CTA)
     static int grid[64];
     if (!grid[dev]) {
-        int rc = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kSmem);
+        int rc = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, S::smem(MT));
         if (rc) return rc;
         int sms = 0, occ = 0;
         if ((rc = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev))) return rc;
-        if ((rc = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, k, S::kThreads, S::kSmem))) return rc;
+        if ((rc = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, k, S::kThreads, S::smem(MT)))) return rc;
         if (occ < 1) return cudaErrorCooperativeLaunchTooLarge;
         grid[dev] = sms;
     }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid[dev]);
     cfg.blockDim = dim3(S::kThreads);
-    cfg.dynamicSmemBytes = S::kSmem;
+    cfg.dynamicSmemBytes = S::smem(a.T);  // 1 <= a.T <= MT (lean_run)
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeCooperative;
@@ -442,8 +464,8 @@ namespace nb {
 
 bool lean_supported(const DecArgs &a) {
     int which = 0;
-    if (a.T < 1 || a.T > kLeanDispatchMaxT || !lean_shape(a, which) || !a.router || a.ep_ranks || a.ep_local)
-        return false;
+    if (a.T < 1 || !lean_shape(a, which) || !a.router || a.ep_ranks || a.ep_local) return false;
+    if (a.T > (which == 0 ? LeanShape<2048, 512, 12>::kMaxT : LeanShape<2560, 640, 20>::kMaxT)) return false;
     int dev = 0, coop = 0;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, dev);
@@ -455,7 +477,10 @@ int lean_run(const DecArgs &a, cudaStream_t st) {
     if (rc) return rc;
     if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
     if (!lean_shape(a, which)) return cudaErrorInvalidValue;
-    return which == 0 ? lean_launch<2048, 512, 12>(a, st, dev) : lean_launch<2560, 640, 20>(a, st, dev);
+    if (a.T < 1 || a.T > (which == 0 ? LeanShape<2048, 512, 12>::kMaxT : LeanShape<2560, 640, 20>::kMaxT))
+        return cudaErrorInvalidValue;
+    if (which == 0) return lean_launch<2048, 512, 12, 2>(a, st, dev);
+    return a.T <= 2 ? lean_launch<2560, 640, 20, 2>(a, st, dev) : lean_launch<2560, 640, 20, 4>(a, st, dev);
 }
 
 }  // namespace nb

@@ -244,10 +244,10 @@ def test_layer_with_shared_expert(L, ref2048, restate, q4k_2048, T):
     assert_parity(out, e_out, f"layer T={T}")
 
 
-@pytest.mark.parametrize("T", (1, 2, 17, 300))
+@pytest.mark.parametrize("T", (1, 2, 3, 4, 17, 300))
 def test_layer_product_shape_with_shared_expert(L, ref2560, restate, prod_2560, T):
     """The production mix at 2560/640 (Q4_K gate/up, IQ4_NL down, IQ4_NL shared
-    down) through the whole layer: the single-kernel layer (1 or 2 tokens), the
+    down) through the whole layer: the single-kernel layer (1 to 4 tokens), the
     tensor-core decode path (T <= 32) and the large-batch path."""
     rng = np.random.default_rng(400 + T)
     x = rng.normal(0, 1, (T, 2560)).astype(np.float32)
