@@ -551,6 +551,42 @@ def single_layer_config(torch, L, peaks, T: int, h: int, f: int, gt: int, dt: in
     return res
 
 
+def product_small_batches(torch, L, peaks, cpu: bool, steps: int) -> dict:
+    """Nebula's production mix (2560/640, Q4_K gate/up + IQ4_NL down, router and
+    shared expert) at T = 1..4 over ROT rotated layers, one graph per T: the range
+    the single-kernel layer takes at this shape. Per T: time per layer, the kernel
+    that ran (per-phase events over one eager pass), the layer's bytes and, with
+    `cpu`, layer 0 of that pass against the reference CPU MoE on the same bytes."""
+    h, f = 2560, 640
+    st = Stack(L, ROT, 4, seed0=15, h=h, f=f, gt=Q4K, dt=IQ4NL, shared=True, bias=False)
+    hl = HostLayers(4, seed0=15, h=h, f=f, gt=Q4K, dt=IQ4NL, shared=True, bias=False) if cpu else None
+    eb = expert_bytes(h, f, Q4K, IQ4NL)
+    pts = {}
+    for t in range(1, 5):
+        g = st.capture(t)
+        for _ in range(3):
+            L.call("graph_launch", g)
+        ms = event_ms(torch, lambda: L.call("graph_launch", g), max(5, steps // 2)) / ROT
+        L.load().qg_graph_destroy(g)
+        used = st.experts_used(t)
+        L.call("moe_profile", 1)
+        st.step(t)
+        prof = read_profile(L)
+        L.call("moe_profile", 0)
+        lb = float(np.mean([layer_bytes(u, t, eb, h, True) for u in used]))
+        pts[str(t)] = {"us_per_layer": ms * 1e3, "tokens_per_s": t / (ms / 1e3),
+                       "experts_used_mean": float(np.mean(used)), "layer_bytes": lb,
+                       "hbm_frac": lb / (ms / 1e3) / 1e9 / peaks["hbm_gbs"],
+                       "kernels": sorted(k for k in prof if prof[k][1])}
+        if hl is not None:
+            out, ids = hl.run(hl.layer(0, t))
+            pts[str(t)]["parity"] = parity(st.w[0]["out"].get()[:t], out, st.w[0]["ids"].get()[:t], ids)
+    del st
+    L.call("sync")
+    return {"workload": f"product shape at T = 1..4: {ROT} rotated layers of 2560/640, Q4_K gate/up + IQ4_NL "
+                        "down, router + shared expert, unbiased routing (graph per T)", "points": pts}
+
+
 def dense_blocks(typ: int, rows: int, cols: int, seed: int) -> np.ndarray:
     """Random Q8_0 (8) or Q6_K (14) rows with valid fp16 scales (the device generator
     covers F32, Q4_K and IQ4_NL)."""
@@ -937,6 +973,7 @@ def main() -> None:
             torch, L, peaks, 17, 2560, 640, Q4K, IQ4NL, True, 13, want_cpu, 3.0,
             "product shape: 1 layer, T=17, hidden 2560 / FFN 640, Q4_K gate/up + IQ4_NL down, router + shared "
             "expert", args.steps, ("tc_experts_kernel<24,1,0>", "product-T17"))
+        configs["product_small_batches"] = product_small_batches(torch, L, peaks, want_cpu, args.steps)
         configs["product_prefill"] = prefill_product(torch, L, peaks, want_cpu, 4.0, args.steps)
         configs["dense_gemv"] = dense_gemv(torch, L, peaks, want_cpu, args.steps)
         sweep = {}
