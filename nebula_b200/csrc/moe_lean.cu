@@ -416,10 +416,14 @@ __global__ void __launch_bounds__(LeanShape<H, F, QD>::kThreads, 1) lean_moe_ker
     }
 }
 
-// Taken up to each shape's kMaxT tokens. Measured on the 48-layer stack (2048/512,
-// Q4_K) it gives 692 / 936 tokens/s at T = 1 / 2 against 358 / 683 for the
-// tensor-core decode path; an earlier build that also took 3 and 4 tokens gave
-// 871 / 931 there, against about 1,000 / 1,300 for the tensor-core path.
+// Taken up to each shape's kMaxT tokens. On the 48-layer stack (2048/512, Q4_K,
+// with the routing skew) it gives 706 / 938 tokens/s at T = 1 / 2 against 356 / 687
+// for the tensor-core decode path, which stays faster at T = 3 and 4 there (1,000 /
+// 1,296 tokens/s). A 4-token instance of this shape took 63.6 / 78.9 us per layer
+// with unbiased routing, against 71.8 / 84.0 us on the tensor-core path; the skew
+// leaves fewer distinct experts, which favours the tensor-core path. At 2560/640 it takes
+// 42.9 / 71.9 / 102.5 / 119.6 us per layer at T = 1..4, against 98.7 / 100.5 /
+// 128.8 / 156.5 us on the tensor-core path (8 rotated layers, graph replay).
 
 bool lean_shape(const DecArgs &a, int &which) {
     if (a.QG != 12) return false;
