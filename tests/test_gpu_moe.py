@@ -260,6 +260,29 @@ def test_layer_product_shape_with_shared_expert(L, ref2560, restate, prod_2560, 
     assert inv == 0 and sel == T * 10 and used == len(np.unique(e_ids))
 
 
+def test_layer_product_small_batches_share_one_workspace(L, ref2560, restate, prod_2560):
+    """The production mix's single-kernel layer has a 2-token and a 4-token
+    instance; both advance the same grid-barrier counter of the workspace. Calls
+    of T = 1, 3, 2, 4, 4, 1 on one workspace (a non-finite token in the fifth)
+    each match the reference: ids bit-exact, outputs within tolerance, status
+    words of that call."""
+    rng = np.random.default_rng(700)
+    ws = L.workspace(4, 2560, 640)
+    for call, T in enumerate((1, 3, 2, 4, 4, 1)):
+        x = rng.normal(0, 1, (T, 2560)).astype(np.float32)
+        if call == 4:
+            x[T - 1, 7] = np.nan
+        out, ids, w, _ = prod_2560.layer(x, ws=ws)
+        n = T - 1 if call == 4 else T  # the finite tokens come first; the checker takes only those
+        e_out, e_ids, e_w, _ = orc.moe_layer(ref2560, restate, x[:n], prod_2560.hrouter, prod_2560.hgate, 12,
+                                             prod_2560.hup, 12, prod_2560.hdown, 20, shared=prod_2560.shared)
+        np.testing.assert_array_equal(ids[:n], e_ids)
+        assert_parity(out[:n], e_out, f"product T={T} call {call}")
+        assert L.status(ws) == (T - n, n * 10, len(np.unique(e_ids)))
+        if n < T:
+            assert np.isnan(out[T - 1]).all() and (ids[T - 1] == -1).all()
+
+
 def test_prefill_product_shape(L, ref2560, restate, prod_2560):
     """Prefill of the production mix: T=2048, N(0,1) logits to top-10."""
     rng = np.random.default_rng(5)
