@@ -330,7 +330,7 @@ class Stack:
         try:
             self.step(T)
         except Exception:
-            self.L.load().qg_graph_destroy(g)
+            self.L.graph_destroy(g)  # abandons the capture
             raise
         self.L.call("graph_end", g)
         return g
@@ -545,7 +545,7 @@ def single_layer_config(torch, L, peaks, T: int, h: int, f: int, gt: int, dt: in
         res["cpu_baseline"] = cpu_line(T / c["per_layer_s"], cores,
                                        f"{c['evals']} evaluations of layers 0-2 (same bytes); qc_moe backend "
                                        f"{c['backend']}")
-    L.load().qg_graph_destroy(g)
+    L.graph_destroy(g)
     del st
     L.call("sync")
     return res
@@ -567,7 +567,7 @@ def product_small_batches(torch, L, peaks, cpu: bool, steps: int) -> dict:
         for _ in range(3):
             L.call("graph_launch", g)
         ms = event_ms(torch, lambda: L.call("graph_launch", g), max(5, steps // 2)) / ROT
-        L.load().qg_graph_destroy(g)
+        L.graph_destroy(g)
         used = st.experts_used(t)
         L.call("moe_profile", 1)
         st.step(t)
@@ -632,7 +632,7 @@ def dense_gemv(torch, L, peaks, cpu: bool, steps: int) -> dict:
             for _ in range(3):
                 L.call("graph_launch", g)
             ms = event_ms(torch, lambda: L.call("graph_launch", g), max(3, steps // 4)) / copies
-            L.load().qg_graph_destroy(g)
+            L.graph_destroy(g)
             nbytes = mb + T * cols * 4 + T * rows * 4
             line[f"T{T}"] = {"us": ms * 1e3, "gbs": nbytes / (ms / 1e3) / 1e9,
                              "hbm_frac": nbytes / (ms / 1e3) / 1e9 / peaks["hbm_gbs"]}
@@ -986,7 +986,7 @@ def main() -> None:
             sb = sum(layer_bytes(x, t) for x in u)
             sweep[str(t)] = {"tokens_per_s": t / (ms_t / 1e3), "ms_per_step": ms_t,
                              "stack_hbm_gbs": sb / (ms_t / 1e3) / 1e9, "experts_used_mean": float(np.mean(u))}
-            L.load().qg_graph_destroy(g)
+            L.graph_destroy(g)
         configs["sweep_T1_17"] = {"workload": "config 3: the 48-layer stack at T = 1..17 (graph per T)",
                                   "points": sweep}
 
@@ -1054,7 +1054,7 @@ def main() -> None:
         line["trace_replay"] = trace_replay
     if rank == 0:
         print(json.dumps(line), flush=True)
-    L.load().qg_graph_destroy(graph)
+    L.graph_destroy(graph)
     if dist:
         dist.barrier()
         stack.epg.close()  # unmap the peers' workspaces before any rank frees its own

@@ -80,15 +80,30 @@ class CudaError(RuntimeError):
         self.code = code
 
 
-# Buffers released while this thread records a graph (qg_graph_begin .. qg_graph_end):
-# a cudaFree then would invalidate the capture, and Python may finalize a buffer at any
-# point (reference cycles are collected whenever the interpreter allocates), so their
-# frees wait until the capture ends.
+# Buffers released while this thread records a graph (qg_graph_begin .. qg_graph_end, or
+# qg_graph_destroy of the graph still recording, which abandons the capture): a cudaFree
+# then would invalidate the capture, and Python may finalize a buffer at any point
+# (reference cycles are collected whenever the interpreter allocates), so their frees wait
+# until the capture ends.
 _capture = threading.local()
 
 
 def _deferring() -> list | None:
     return getattr(_capture, "pending", None)
+
+
+def _handle_written(arg):
+    """The graph handle qg_graph_begin wrote through C.byref(g) or C.pointer(g)."""
+    obj = getattr(arg, "_obj", None)
+    if obj is None:
+        obj = getattr(arg, "contents", None)
+    return getattr(obj, "value", None)
+
+
+def _end_capture(lib) -> None:
+    pending, _capture.pending, _capture.graph = _deferring() or [], None, None
+    for p in pending:
+        lib.qg_free(p)
 
 
 def call(name: str, *args) -> None:
@@ -97,12 +112,21 @@ def call(name: str, *args) -> None:
     code = getattr(lib, "qg_" + name)(*args)
     if name == "graph_begin" and not code:
         _capture.pending = []
+        _capture.graph = _handle_written(args[0])
     elif name == "graph_end":
-        pending, _capture.pending = _deferring() or [], None
-        for p in pending:
-            lib.qg_free(p)
+        _end_capture(lib)
     if code:
         raise CudaError(name, code, lib.qg_error(code).decode())
+
+
+def graph_destroy(graph) -> None:
+    """qg_graph_destroy (a ``c_void_p`` or an int handle). Destroying the graph this
+    thread is still recording ends that capture, and the frees it deferred run."""
+    lib = load()
+    h = graph.value if isinstance(graph, C.c_void_p) else graph
+    lib.qg_graph_destroy(h)
+    if _deferring() is not None and h is not None and getattr(_capture, "graph", None) == h:
+        _end_capture(lib)
 
 
 def code(name: str, *args) -> int:
