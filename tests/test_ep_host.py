@@ -1,5 +1,6 @@
 """Expert-parallel host logic on CPU: placement and the handle exchange over
-gloo with two ranks (no GPU)."""
+gloo with two ranks (no GPU), including a rank that sends a malformed handle and
+a rank that never joins (both end in an error on the other rank, not a hang)."""
 import os
 import socket
 
@@ -73,3 +74,40 @@ def test_handle_exchange_gloo(bad_rank):
     else:
         assert results[bad_rank] == "sent-bad"
         assert str(results[0]).startswith("error:")
+
+
+def _absent_worker(rank, world, port, results):
+    """Rank 1 never joins the exchange; rank 0's exchange must end with an error
+    within the process group's timeout instead of waiting for good."""
+    import time
+    from datetime import timedelta
+
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"], os.environ["MASTER_PORT"] = "127.0.0.1", str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=5))
+    try:
+        if rank == 1:
+            t_end = time.monotonic() + 120
+            while 0 not in results and time.monotonic() < t_end:
+                time.sleep(0.1)
+            results[1] = "absent"
+            return
+        t0 = time.monotonic()
+        try:
+            ep.exchange_handles(bytes(ep.IPC_HANDLE_BYTES), world)
+            results[0] = "returned"
+        except RuntimeError as e:
+            results[0] = ("error", time.monotonic() - t0, type(e).__name__)
+    finally:
+        dist.destroy_process_group()
+
+
+def test_handle_exchange_with_an_absent_rank_times_out():
+    world = 2
+    mgr = mp.get_context("spawn").Manager()
+    results = mgr.dict()
+    mp.start_processes(_absent_worker, args=(world, _free_port(), results), nprocs=world,
+                       start_method="spawn", join=True)
+    assert results[1] == "absent"
+    kind, waited, _ = results[0]
+    assert kind == "error" and waited < 60
